@@ -1,0 +1,69 @@
+"""ctypes binding of ``libcvhrf.so`` (the C ABI declared in ``include/cvhrf.h``).
+
+The CUDA library is the only implementation: if it is missing or cannot be
+loaded, every operator raises instead of falling back to another path.
+"""
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcvhrf.so")
+_lock = threading.Lock()
+_lib = None
+
+c_int, c_float, c_size_t, c_void_p = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p
+c_float_p = ctypes.POINTER(ctypes.c_float)
+
+# name -> (restype, argtypes); must match include/cvhrf.h
+SIGNATURES = {
+    "cvhrf_status_string": (ctypes.c_char_p, [c_int]),
+    "cvhrf_last_cuda_error": (c_int, []),
+    "cvhrf_version": (c_int, []),
+    "cvhrf_asm_plan_create": (c_int, [c_int, ctypes.POINTER(c_void_p)]),
+    "cvhrf_asm_plan_destroy": (c_int, [c_void_p]),
+    "cvhrf_asm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),
+    "cvhrf_asm_propagate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_int,
+                                    c_float, c_float, c_float, c_float, c_int, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_asm_propagate_planes": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float_p, c_float_p,
+                                           c_float, c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_asm_propagate_planes_adjoint": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float_p,
+                                                   c_float_p, c_float, c_float, c_void_p, c_void_p, c_size_t,
+                                                   c_void_p]),
+}
+
+
+class CvhrfError(RuntimeError):
+    pass
+
+
+def lib():
+    """Load (once) and return the CUDA library; raises if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise CvhrfError(
+                    f"{LIB_PATH} is missing: build it with "
+                    "`python -m complex_valued_holographic_radiance_fields_b200.build` (no CPU fallback exists)")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def check(status, what):
+    if status != 0:
+        L = lib()
+        msg = L.cvhrf_status_string(status).decode()
+        raise CvhrfError(f"{what} failed: {msg} (status {status}, cuda error {L.cvhrf_last_cuda_error()})")
+
+
+def float_array(values):
+    vals = [float(v) for v in values]
+    return (ctypes.c_float * len(vals))(*vals)

@@ -1,0 +1,443 @@
+// Band-limited angular-spectrum propagation fused into a hand-written FFT.
+//
+// Reference path (cuda_prop/python_function.py:109-218): zero_pad to 2S x 2S ->
+// torch.fft.fft2 -> fftshift -> bandlimited_propagation_{forward,backward}_kernel
+// (cuda/bandlimited_propagation_cuda.cu:29-147) -> ifftshift -> ifft2 -> crop.
+// Here the same operator runs as three passes over HBM:
+//
+//   A (rows, forward):   each of the Hi non-zero input rows -> length-2S spectrum
+//   B (columns):         each spectrum column: forward FFT, x transfer x aperture,
+//                        inverse FFT, keep only the Ho cropped rows
+//   C (rows, inverse):   each kept row: inverse FFT, keep the Wo cropped columns, / (2S)^2
+//
+// A length-2S transform of a zero-padded line is done as two length-S transforms
+// (even and odd output bins): X[2m] = FFT_S(wrap(x))[m] and
+// X[2m+1] = FFT_S(wrap(x * w_{2S}^n))[m], where wrap folds padded index n to n mod S
+// (the non-zero window is never longer than S, so no two samples collide).  The
+// inverse with a crop of at most S outputs folds back the same way:
+// y[n] = e[n mod S] + w_{2S}^{-n} f[n mod S].  fftshift/ifftshift never move data:
+// the transfer function is evaluated at each bin's shifted coordinates instead.
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+#include "common.cuh"
+#include "fft_lines.cuh"
+
+namespace cvhrf {
+
+struct TransferParams {
+  float k;          // (float)(2 pi / lambda), computed in double as the reference host code does
+  float distance;
+  float fx_max, fy_max;
+  float inv_np;     // (float)(1 / (P * pitch)): torch.fft.fftfreq scale
+  float aperture;   // radius in shifted index space; <= 0 disables
+  float offset_x, offset_y;
+};
+
+// Per-launch list of column jobs (one job = one input spectrum item -> one output item).
+constexpr int kMaxJobs = 32;
+struct ColumnJobs {
+  int n;
+  int in_item[kMaxJobs];
+  int out_item[kMaxJobs];
+  TransferParams tp[kMaxJobs];
+};
+
+// Host-side constants of bandlimited_propagation_cuda.cu:149-170 (float arithmetic,
+// k via double), for a square padded grid of side P.
+static TransferParams make_transfer(float wavelength, float pitch, float distance, float aperture, int P) {
+  TransferParams t;
+  t.k = (float)(2.0f * M_PI / wavelength);
+  const float x_size = pitch * P;
+  const float y_size = pitch * P;
+  const float ax = 2.0f * distance * (1.0f / x_size);
+  const float ay = 2.0f * distance * (1.0f / y_size);
+  t.fx_max = 1.0f / sqrtf(ax * ax + 1.0f) / wavelength;
+  t.fy_max = 1.0f / sqrtf(ay * ay + 1.0f) / wavelength;
+  t.distance = distance;
+  t.inv_np = (float)(1.0 / ((double)P * (double)pitch));
+  t.aperture = aperture;
+  t.offset_x = P / 2.0f - 0.5f;
+  t.offset_y = P / 2.0f - 0.5f;
+  return t;
+}
+
+// Transfer function x aperture at unshifted bin (ku = row, kv = column) of a P x P
+// grid.  Row bins carry FX (meshgrid 'ij', python_function.py:137-142), column bins FY.
+// The expressions follow bandlimited_propagation_cuda.cu:50-85 term by term (kz^2 in
+// double, stored to float, sqrtf, phase = d*kz, accurate sincosf); the aperture test is
+// on shifted indices (i + P/2) mod P.
+__device__ __forceinline__ float2 transfer_at(int ku, int kv, int P, const TransferParams& tp) {
+  const int half = P >> 1;
+  const float fx_val = __fmul_rn((float)(ku < half ? ku : ku - P), tp.inv_np);
+  const float fy_val = __fmul_rn((float)(kv < half ? kv : kv - P), tp.inv_np);
+  const bool within_bandlimit = (fabsf(fx_val) < tp.fx_max) && (fabsf(fy_val) < tp.fy_max);
+  const float k = tp.k;
+  const float kz_squared = k * k - (2 * M_PI * fx_val) * (2 * M_PI * fx_val) - (2 * M_PI * fy_val) * (2 * M_PI * fy_val);
+  float2 tr = make_float2(0.0f, 0.0f);
+  if (kz_squared > 0.0f && within_bandlimit) {
+    const float kz = sqrtf(kz_squared);
+    const float phase = tp.distance * kz;
+    float s, c;
+    sincosf(phase, &s, &c);
+    tr = make_float2(c, s);
+  }
+  if (tp.aperture > 0.0f) {
+    const int idx = (kv + half) % P;  // shifted column index
+    const int idy = (ku + half) % P;  // shifted row index
+    const float x = (float)idx - tp.offset_x;
+    const float y = (float)idy - tp.offset_y;
+    const float r = tp.aperture;
+    const float m = (x * x + y * y < r * r) ? 1.0f : 0.0f;
+    tr.x *= m;
+    tr.y *= m;
+  }
+  return tr;
+}
+
+// ---- pass A: forward row transforms ------------------------------------------------
+// in: items x Hi x Wi; A: items x Hi x P, each row in split digit-reversed bin order
+// [even bins | odd bins].  One CTA handles `rows` consecutive rows (2 lines per row).
+__global__ void __launch_bounds__(512) asm_rows_forward_kernel(
+    const float2* __restrict__ in, int total_rows, int Wi, float2* __restrict__ A, FftDesc d, int rows) {
+  extern __shared__ float2 sm[];
+  const int S = d.S, P = 2 * S;
+  const int ow = (P - Wi) / 2;
+  const int row0 = blockIdx.x * rows;
+  const int nrows = min(rows, total_rows - row0);
+  if (nrows <= 0) return;
+  // fill: position t of the even line takes padded index t or t+S, whichever is inside
+  for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
+    const int r = e / S, t = e - r * S;
+    const float2* src = in + (size_t)(row0 + r) * Wi;
+    int pos = t;
+    int j = pos - ow;
+    if (j < 0 || j >= Wi) { pos = t + S; j = pos - ow; }
+    float2 v = make_float2(0.f, 0.f), vo = v;
+    if (j >= 0 && j < Wi) {
+      v = src[j];
+      vo = cmul(v, __ldg(&d.twP[pos]));
+    }
+    sm[(2 * r) * S + t] = v;
+    sm[(2 * r + 1) * S + t] = vo;
+  }
+  __syncthreads();
+  fft_forward_lines(sm, 2 * nrows, S, d);
+  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
+    const int r = e / P, q = e - r * P;
+    A[(size_t)(row0 + r) * P + q] = sm[(2 * r) * S + q];  // lines 2r, 2r+1 are contiguous
+  }
+}
+
+// ---- pass B: column transforms with the transfer function --------------------------
+// A: in_items x Hi x P; B: out_items x Ho x P.  CTA = `cols` consecutive columns of one job.
+__global__ void __launch_bounds__(512) asm_columns_kernel(
+    const float2* __restrict__ A, int Hi, float2* __restrict__ B, int Ho, FftDesc d, int cols,
+    ColumnJobs jobs, int accumulate) {
+  extern __shared__ float2 sm[];
+  const int S = d.S, P = 2 * S;
+  const int job = blockIdx.y;
+  const int q0 = blockIdx.x * cols;
+  const int ncols = min(cols, P - q0);
+  const float2* Ain = A + (size_t)jobs.in_item[job] * Hi * P;
+  float2* Bout = B + (size_t)jobs.out_item[job] * Ho * P;
+  const TransferParams tp = jobs.tp[job];
+  const int oh = (P - Hi) / 2;
+  // lines: column c, half h -> line 2c + h
+  for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+    const int t = e / ncols, c = e - t * ncols;
+    int pos = t;
+    int r = pos - oh;
+    if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
+    float2 v = make_float2(0.f, 0.f), vo = v;
+    if (r >= 0 && r < Hi) {
+      v = Ain[(size_t)r * P + q0 + c];
+      vo = cmul(v, __ldg(&d.twP[pos]));
+    }
+    sm[(2 * c) * S + t] = v;
+    sm[(2 * c + 1) * S + t] = vo;
+  }
+  __syncthreads();
+  fft_forward_lines(sm, 2 * ncols, S, d);
+  for (int e = threadIdx.x; e < 2 * ncols * S; e += blockDim.x) {
+    const int line = e / S, pos = e - line * S;
+    const int c = line >> 1, h = line & 1;
+    const int q = q0 + c;
+    const int qh = q >= S ? 1 : 0;
+    const int kv = 2 * __ldg(&d.digrev[q - qh * S]) + qh;
+    const int ku = 2 * __ldg(&d.digrev[pos]) + h;
+    sm[e] = cmul(sm[e], transfer_at(ku, kv, P, tp));
+  }
+  __syncthreads();
+  fft_inverse_lines(sm, 2 * ncols, S, d);
+  const int oc = (P - Ho) / 2;
+  for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+    const int rr = e / ncols, c = e - rr * ncols;
+    const int n = oc + rr;
+    const int t = n >= S ? n - S : n;
+    const float2 ev = sm[(2 * c) * S + t];
+    const float2 od = sm[(2 * c + 1) * S + t];
+    float2 v = cadd(ev, cmul(cconj(__ldg(&d.twP[n])), od));
+    float2* dst = Bout + (size_t)rr * P + q0 + c;
+    if (accumulate) { float2 o = *dst; v = cadd(o, v); }
+    *dst = v;
+  }
+}
+
+// ---- pass C: inverse row transforms + crop + 1/P^2 ---------------------------------
+__global__ void __launch_bounds__(512) asm_rows_inverse_kernel(
+    const float2* __restrict__ B, int total_rows, float2* __restrict__ out, int Wo, FftDesc d, int rows,
+    float scale, int accumulate) {
+  extern __shared__ float2 sm[];
+  const int S = d.S, P = 2 * S;
+  const int row0 = blockIdx.x * rows;
+  const int nrows = min(rows, total_rows - row0);
+  if (nrows <= 0) return;
+  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
+    const int r = e / P, q = e - r * P;
+    sm[(2 * r) * S + q] = B[(size_t)(row0 + r) * P + q];
+  }
+  __syncthreads();
+  fft_inverse_lines(sm, 2 * nrows, S, d);
+  const int oc = (P - Wo) / 2;
+  for (int e = threadIdx.x; e < nrows * Wo; e += blockDim.x) {
+    const int r = e / Wo, x = e - r * Wo;
+    const int n = oc + x;
+    const int t = n >= S ? n - S : n;
+    const float2 ev = sm[(2 * r) * S + t];
+    const float2 od = sm[(2 * r + 1) * S + t];
+    float2 v = cadd(ev, cmul(cconj(__ldg(&d.twP[n])), od));
+    v.x *= scale;
+    v.y *= scale;
+    float2* dst = out + (size_t)(row0 + r) * Wo + x;
+    if (accumulate) { float2 o = *dst; v = cadd(o, v); }
+    *dst = v;
+  }
+}
+
+}  // namespace cvhrf
+
+// ---------------------------------------------------------------------------------
+using namespace cvhrf;
+
+struct cvhrf_asm_plan {
+  FftDesc desc;
+  void* dev_mem;
+  int device;
+};
+
+static bool factorize(int S, FftDesc& d) {
+  int n = S, a = 0;
+  while (n % 2 == 0) { n /= 2; ++a; }
+  int b = 0; while (n % 3 == 0) { n /= 3; ++b; }
+  int c = 0; while (n % 5 == 0) { n /= 5; ++c; }
+  if (n != 1) return false;
+  std::vector<int> r;
+  int n8 = a / 3, rem = a % 3;
+  if (rem == 1 && n8 >= 1) { n8 -= 1; for (int i = 0; i < n8; ++i) r.push_back(8); r.push_back(4); r.push_back(4); }
+  else { for (int i = 0; i < n8; ++i) r.push_back(8); if (rem == 1) r.push_back(2); if (rem == 2) r.push_back(4); }
+  for (int i = 0; i < b; ++i) r.push_back(3);
+  for (int i = 0; i < c; ++i) r.push_back(5);
+  if ((int)r.size() > kMaxFftStages) return false;
+  d.S = S;
+  d.nst = (int)r.size();
+  int L = S;
+  for (int i = 0; i < d.nst; ++i) {
+    d.radix[i] = r[i];
+    L /= r[i];
+    d.L[i] = L;
+    d.span[i] = S / (r[i] * L);
+  }
+  return true;
+}
+
+extern "C" int cvhrf_asm_plan_create(int S, cvhrf_asm_plan** plan_out) {
+  if (!plan_out || S < 8 || S > 4096) return CVHRF_EINVAL;
+  FftDesc d{};
+  if (!factorize(S, d)) return CVHRF_EUNSUPPORTED;
+  const int P = 2 * S;
+  std::vector<float2> tw(S), twP(P);
+  for (int t = 0; t < S; ++t) {
+    double a = -2.0 * M_PI * (double)t / (double)S;
+    tw[t] = make_float2((float)cos(a), (float)sin(a));
+  }
+  for (int t = 0; t < P; ++t) {
+    double a = -2.0 * M_PI * (double)t / (double)P;
+    twP[t] = make_float2((float)cos(a), (float)sin(a));
+  }
+  // digit reversal: bin k = m1 + R1 (m2 + R2 (...)) sits at position sum_i L_i m_i
+  std::vector<int> digrev(S);
+  for (int k = 0; k < S; ++k) {
+    int rem = k, pos = 0;
+    for (int i = 0; i < d.nst; ++i) {
+      int m = rem % d.radix[i];
+      rem /= d.radix[i];
+      pos += d.L[i] * m;
+    }
+    digrev[pos] = k;
+  }
+  size_t bytes = (size_t)(S + P) * sizeof(float2) + (size_t)S * sizeof(int);
+  cvhrf_asm_plan* plan = (cvhrf_asm_plan*)calloc(1, sizeof(cvhrf_asm_plan));
+  if (!plan) return CVHRF_EINVAL;
+  CVHRF_CUDA_TRY(cudaGetDevice(&plan->device));
+  cudaError_t e = cudaMalloc(&plan->dev_mem, bytes);
+  if (e != cudaSuccess) { free(plan); set_last_cuda_error((int)e); return CVHRF_ECUDA; }
+  char* base = (char*)plan->dev_mem;
+  e = cudaMemcpy(base, tw.data(), S * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(base + S * sizeof(float2), twP.data(), P * sizeof(float2), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(base + (S + P) * sizeof(float2), digrev.data(), S * sizeof(int), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) { cudaFree(plan->dev_mem); free(plan); set_last_cuda_error((int)e); return CVHRF_ECUDA; }
+  d.tw = (const float2*)base;
+  d.twP = (const float2*)(base + S * sizeof(float2));
+  d.digrev = (const int*)(base + (S + P) * sizeof(float2));
+  plan->desc = d;
+  *plan_out = plan;
+  return CVHRF_OK;
+}
+
+extern "C" int cvhrf_asm_plan_destroy(cvhrf_asm_plan* plan) {
+  if (!plan) return CVHRF_OK;
+  cudaFree(plan->dev_mem);
+  free(plan);
+  return CVHRF_OK;
+}
+
+static const size_t kSmemBudget = 100 * 1024;
+
+static size_t ws_bytes_impl(int S, int in_items, int Hi, int out_items, int Ho) {
+  const size_t P = 2 * (size_t)S;
+  return align_up((size_t)in_items * Hi * P * sizeof(float2), 256) + align_up((size_t)out_items * Ho * P * sizeof(float2), 256);
+}
+
+extern "C" size_t cvhrf_asm_workspace_bytes(int S, int items, int Hi, int Wi, int out_items, int Ho, int Wo) {
+  (void)Wi; (void)Wo;
+  return ws_bytes_impl(S, items, Hi, out_items, Ho);
+}
+
+namespace {
+
+int rows_per_cta(int S) {
+  int r = (int)(kSmemBudget / (2 * (size_t)S * sizeof(float2)));
+  return r < 1 ? 1 : (r > 16 ? 16 : r);
+}
+
+int launch_rows_forward(const FftDesc& d, const float2* in, int total_rows, int Wi, float2* A, cudaStream_t st) {
+  const int rows = rows_per_cta(d.S);
+  const size_t smem = (size_t)rows * 2 * d.S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(asm_rows_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((total_rows + rows - 1) / rows);
+  asm_rows_forward_kernel<<<grid, 512, smem, st>>>(in, total_rows, Wi, A, d, rows);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+int launch_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho, const ColumnJobs& jobs,
+                   int accumulate, cudaStream_t st) {
+  const int P = 2 * d.S;
+  const int cols = rows_per_cta(d.S);
+  const size_t smem = (size_t)cols * 2 * d.S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(asm_columns_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((P + cols - 1) / cols, jobs.n);
+  asm_columns_kernel<<<grid, 512, smem, st>>>(A, Hi, B, Ho, d, cols, jobs, accumulate);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+int launch_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float2* out, int Wo, int accumulate,
+                        cudaStream_t st) {
+  const int rows = rows_per_cta(d.S);
+  const size_t smem = (size_t)rows * 2 * d.S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(asm_rows_inverse_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const float P = 2.0f * d.S;
+  const float scale = 1.0f / (P * P);
+  dim3 grid((total_rows + rows - 1) / rows);
+  asm_rows_inverse_kernel<<<grid, 512, smem, st>>>(B, total_rows, out, Wo, d, rows, scale, accumulate);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+bool dims_ok(int S, int H, int W) { return H >= 1 && W >= 1 && H <= S && W <= S; }
+
+}  // namespace
+
+extern "C" int cvhrf_asm_propagate(const cvhrf_asm_plan* plan, const void* in, int Hi, int Wi, void* out, int Ho,
+                                   int Wo, float wavelength, float pixel_pitch, float distance, float aperture,
+                                   int accumulate, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!plan || !in || !out) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (!dims_ok(d.S, Hi, Wi) || !dims_ok(d.S, Ho, Wo)) return CVHRF_EINVAL;
+  if (!(wavelength > 0.0f) || !(pixel_pitch > 0.0f)) return CVHRF_EINVAL;
+  Carver cv(workspace, workspace_bytes);
+  const int P = 2 * d.S;
+  float2* A = cv.take<float2>((size_t)Hi * P);
+  float2* B = cv.take<float2>((size_t)Ho * P);
+  if (cv.overflow) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = launch_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
+  ColumnJobs jobs{};
+  jobs.n = 1;
+  jobs.in_item[0] = 0;
+  jobs.out_item[0] = 0;
+  jobs.tp[0] = make_transfer(wavelength, pixel_pitch, distance, aperture, P);
+  if ((rc = launch_columns(d, A, Hi, B, Ho, jobs, 0, st))) return rc;
+  return launch_rows_inverse(d, B, Ho, (float2*)out, Wo, accumulate, st);
+}
+
+extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void* fields, int K, int C, int H, int W,
+                                          const float* wavelengths, const float* distances, float pixel_pitch,
+                                          float aperture, void* holo, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+  if (!plan || !fields || !holo || !wavelengths || !distances) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (K < 1 || C < 1 || K * C > kMaxJobs || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
+  const int S = d.S, P = 2 * S;
+  Carver cv(workspace, workspace_bytes);
+  float2* A = cv.take<float2>((size_t)K * C * H * P);
+  float2* B = cv.take<float2>((size_t)C * S * P);
+  if (cv.overflow) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = launch_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
+  for (int p = 0; p < K; ++p) {
+    ColumnJobs jobs{};
+    jobs.n = C;
+    for (int c = 0; c < C; ++c) {
+      if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+      jobs.in_item[c] = p * C + c;
+      jobs.out_item[c] = c;
+      jobs.tp[c] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
+    }
+    if ((rc = launch_columns(d, A, H, B, S, jobs, p > 0 ? 1 : 0, st))) return rc;
+  }
+  return launch_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+}
+
+extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, const void* grad_holo, int K, int C,
+                                                  int H, int W, const float* wavelengths, const float* distances,
+                                                  float pixel_pitch, float aperture, void* grad_fields,
+                                                  void* workspace, size_t workspace_bytes, void* stream) {
+  if (!plan || !grad_holo || !grad_fields || !wavelengths || !distances) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (K < 1 || C < 1 || K * C > kMaxJobs || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
+  const int S = d.S, P = 2 * S;
+  Carver cv(workspace, workspace_bytes);
+  float2* A = cv.take<float2>((size_t)C * S * P);
+  float2* B = cv.take<float2>((size_t)K * C * H * P);
+  if (cv.overflow) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = launch_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
+  ColumnJobs jobs{};
+  jobs.n = K * C;
+  for (int p = 0; p < K; ++p)
+    for (int c = 0; c < C; ++c) {
+      if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+      jobs.in_item[p * C + c] = c;
+      jobs.out_item[p * C + c] = p * C + c;
+      jobs.tp[p * C + c] = make_transfer(wavelengths[c], pixel_pitch, -distances[p], aperture, P);
+    }
+  if ((rc = launch_columns(d, A, S, B, H, jobs, 0, st))) return rc;
+  return launch_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+}

@@ -1,0 +1,50 @@
+// Shared helpers for the cvhrf CUDA sources: status plumbing and small math.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+#include "../../include/cvhrf.h"
+
+namespace cvhrf {
+
+// Records the failing cudaError_t for cvhrf_last_cuda_error() (defined in capi.cu).
+void set_last_cuda_error(int err);
+
+#define CVHRF_CUDA_TRY(expr)                                    \
+  do {                                                          \
+    cudaError_t _e = (expr);                                    \
+    if (_e != cudaSuccess) {                                    \
+      ::cvhrf::set_last_cuda_error((int)_e);                    \
+      return CVHRF_ECUDA;                                       \
+    }                                                           \
+  } while (0)
+
+#define CVHRF_LAUNCH_CHECK() CVHRF_CUDA_TRY(cudaGetLastError())
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Carves 256-byte aligned sub-buffers out of a caller-provided workspace.
+struct Carver {
+  char* base;
+  size_t cap;
+  size_t used = 0;
+  bool overflow = false;
+  Carver(void* b, size_t c) : base((char*)b), cap(c) {}
+  template <typename T>
+  T* take(size_t count) {
+    size_t off = align_up(used, 256);
+    size_t bytes = count * sizeof(T);
+    used = off + bytes;
+    if (used > cap || (base == nullptr && count > 0)) { overflow = true; return nullptr; }
+    return reinterpret_cast<T*>(base + off);
+  }
+};
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(a.x * b.x - a.y * b.y, a.x * b.y + a.y * b.x);
+}
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cconj(float2 a) { return make_float2(a.x, -a.y); }
+
+}  // namespace cvhrf

@@ -1,0 +1,162 @@
+"""Band-limited angular-spectrum propagation (the ``cuda_prop`` operator surface).
+
+Mirrors ``cuda_prop/python_function.py``:
+
+* ``BandlimitedPropagationFunction.apply(field, wavelength, pixel_pitch, distance,
+  size, aperture_size=-1.0)`` (python_function.py:109-218) — one field, forward is
+  ``crop_S(IFFT2(H * A * FFT2(pad_2S(field))))`` and backward its exact adjoint.
+* ``BandlimitedPropagation(field, wavelength, pixel_pitch, distance, size, use_cuda,
+  aperture_size=-1.0)`` (python_function.py:220-226).
+* ``PlanePropagationFunction`` — the K-plane x C-channel loop of model.py:1251-1272
+  (``hologram = sum_p stack_c BandlimitedPropagation(field[p, c], lambda_c, ..., -d_p)``)
+  as one fused operator.
+
+All arithmetic runs in ``libcvhrf.so`` (hand-written sm_100a FFT fused with the
+transfer function); torch only provides device memory and the current stream.
+"""
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+_plans = {}
+_plans_lock = threading.Lock()
+
+
+def get_plan(S, device):
+    """Twiddle/digit-reversal tables for padded size 2S on `device` (created once)."""
+    dev = torch.device(device)
+    key = (int(S), dev.index if dev.index is not None else torch.cuda.current_device())
+    with _plans_lock:
+        p = _plans.get(key)
+        if p is None:
+            L = _lib.lib()
+            h = ctypes.c_void_p()
+            with torch.cuda.device(key[1]):
+                _lib.check(L.cvhrf_asm_plan_create(int(S), ctypes.byref(h)), f"asm plan (S={S})")
+            p = _plans[key] = h
+    return p
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _square_size(size):
+    if isinstance(size, int):
+        return int(size)
+    size = [int(s) for s in size]
+    if len(size) != 2 or size[0] != size[1]:
+        # The reference kernel indexes idy*nx+idx (bandlimited_propagation_cuda.cu:54),
+        # which is only correct for square padded grids; all its call sites pass [S, S].
+        raise ValueError(f"size must be [S, S] (square), got {size}")
+    return size[0]
+
+
+def _check_field(x, name):
+    if not x.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor (libcvhrf has no CPU path)")
+    if x.dtype != torch.complex64:
+        raise TypeError(f"{name} must be complex64, got {x.dtype}")
+    return x.contiguous()
+
+
+def _scalar(v):
+    return float(v.item()) if torch.is_tensor(v) else float(v)
+
+
+def _workspace(S, in_items, Hi, out_items, Ho, device):
+    nbytes = _lib.lib().cvhrf_asm_workspace_bytes(S, in_items, Hi, 0, out_items, Ho, 0)
+    return torch.empty(max(int(nbytes), 1), dtype=torch.uint8, device=device)
+
+
+def propagate(field, wavelength, pixel_pitch, distance, S, aperture_size=-1.0, out_hw=None, out=None,
+              accumulate=False):
+    """Single propagation: field (Hi, Wi) complex64 -> out (Ho, Wo) (default S x S)."""
+    field = _check_field(field, "field")
+    if field.dim() != 2:
+        raise ValueError("field must be 2-D (H, W)")
+    Hi, Wi = field.shape
+    Ho, Wo = (S, S) if out_hw is None else out_hw
+    if out is None:
+        out = torch.empty((Ho, Wo), dtype=torch.complex64, device=field.device)
+    ws = _workspace(S, 1, Hi, 1, Ho, field.device)
+    L = _lib.lib()
+    st = L.cvhrf_asm_propagate(get_plan(S, field.device), ctypes.c_void_p(field.data_ptr()), Hi, Wi,
+                               ctypes.c_void_p(out.data_ptr()), Ho, Wo, _scalar(wavelength), _scalar(pixel_pitch),
+                               _scalar(distance), _scalar(aperture_size), int(bool(accumulate)),
+                               ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(field))
+    _lib.check(st, "cvhrf_asm_propagate")
+    return out
+
+
+class BandlimitedPropagationFunction(torch.autograd.Function):
+    """python_function.py:109-218 — same arguments, same return, same gradients."""
+
+    @staticmethod
+    def forward(ctx, field, wavelength, pixel_pitch, distance, size, aperture_size=-1.0):
+        S = _square_size(size)
+        ctx.params = (_scalar(wavelength), _scalar(pixel_pitch), _scalar(distance), S, _scalar(aperture_size))
+        ctx.input_size = tuple(field.shape[-2:])
+        return propagate(field, *ctx.params[:3], S, ctx.params[4])
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        wl, pitch, dist, S, ap = ctx.params
+        grad_field = propagate(grad_output.contiguous(), wl, pitch, -dist, S, ap, out_hw=ctx.input_size)
+        return grad_field, None, None, None, None, None
+
+
+def BandlimitedPropagation(field, wavelength, pixel_pitch, distance, size, use_cuda=True, aperture_size=-1.0):
+    """python_function.py:220-226.  Only the CUDA path exists in this package."""
+    if not use_cuda:
+        raise NotImplementedError("use_cuda=False (the pure-torch CPU path) is not part of this package")
+    return BandlimitedPropagationFunction.apply(field, wavelength, pixel_pitch, distance, size, aperture_size)
+
+
+class PlanePropagationFunction(torch.autograd.Function):
+    """Fused plane/channel loop of model.py:1251-1272.
+
+    fields (K, C, H, W) complex64 -> hologram (C, S, S) = sum_p propagate(fields[p, c],
+    wavelengths[c], distances[p]).  `distances` are the signed distances passed to
+    BandlimitedPropagation (the model passes -d_p).
+    """
+
+    @staticmethod
+    def forward(ctx, fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0):
+        fields = _check_field(fields, "fields")
+        K, C, H, W = fields.shape
+        wl = [_scalar(w) for w in wavelengths]
+        ds = [_scalar(d) for d in distances]
+        if len(wl) != C or len(ds) != K:
+            raise ValueError("len(wavelengths) must equal C and len(distances) must equal K")
+        ctx.cfg = (wl, ds, _scalar(pixel_pitch), int(S), _scalar(aperture_size), (K, C, H, W))
+        holo = torch.empty((C, S, S), dtype=torch.complex64, device=fields.device)
+        ws = _workspace(S, K * C, H, C, S, fields.device)
+        L = _lib.lib()
+        st = L.cvhrf_asm_propagate_planes(get_plan(S, fields.device), ctypes.c_void_p(fields.data_ptr()), K, C, H,
+                                          W, _lib.float_array(wl), _lib.float_array(ds), ctx.cfg[2], ctx.cfg[4],
+                                          ctypes.c_void_p(holo.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                          ws.numel(), _stream(fields))
+        _lib.check(st, "cvhrf_asm_propagate_planes")
+        return holo
+
+    @staticmethod
+    def backward(ctx, grad_holo):
+        wl, ds, pitch, S, ap, (K, C, H, W) = ctx.cfg
+        g = _check_field(grad_holo, "grad_holo")
+        grad_fields = torch.empty((K, C, H, W), dtype=torch.complex64, device=g.device)
+        ws = _workspace(S, C, S, K * C, H, g.device)
+        L = _lib.lib()
+        st = L.cvhrf_asm_propagate_planes_adjoint(get_plan(S, g.device), ctypes.c_void_p(g.data_ptr()), K, C, H, W,
+                                                  _lib.float_array(wl), _lib.float_array(ds), pitch, ap,
+                                                  ctypes.c_void_p(grad_fields.data_ptr()),
+                                                  ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(g))
+        _lib.check(st, "cvhrf_asm_propagate_planes_adjoint")
+        return grad_fields, None, None, None, None, None
+
+
+def propagate_planes(fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0):
+    return PlanePropagationFunction.apply(fields, wavelengths, distances, pixel_pitch, S, aperture_size)
