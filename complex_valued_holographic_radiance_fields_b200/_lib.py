@@ -30,7 +30,23 @@ SIGNATURES = {
     "cvhrf_asm_propagate_planes_adjoint": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float_p,
                                                    c_float_p, c_float, c_float, c_void_p, c_void_p, c_size_t,
                                                    c_void_p]),
+    "cvhrf_raster_geometry_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "cvhrf_raster_forward_geometry": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "cvhrf_raster_binning_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "cvhrf_raster_forward_render": (c_int, [c_void_p, c_void_p, c_size_t, c_int, c_int, c_void_p, c_size_t,
+                                            c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "cvhrf_raster_backward_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "cvhrf_raster_backward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 9),
 }
+
+
+class RasterScene(ctypes.Structure):
+    """cvhrf_raster_scene (include/cvhrf.h)."""
+    _fields_ = [(n, c_int) for n in ("N", "K", "C", "W", "H")] + \
+               [(n, c_float) for n in ("fx", "fy", "px", "py", "near_plane", "far_plane")] + \
+               [(n, c_void_p) for n in ("cam_means", "z_vals", "quats", "scales", "colours", "phase", "opacities",
+                                        "plane_probs", "view_matrix")]
 
 
 class CvhrfError(RuntimeError):

@@ -372,7 +372,7 @@ extern "C" int cvhrf_asm_propagate(const cvhrf_asm_plan* plan, const void* in, i
   const int P = 2 * d.S;
   float2* A = cv.take<float2>((size_t)Hi * P);
   float2* B = cv.take<float2>((size_t)Ho * P);
-  if (cv.overflow) return CVHRF_EWORKSPACE;
+  if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   if ((rc = launch_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
@@ -396,7 +396,7 @@ extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void
   Carver cv(workspace, workspace_bytes);
   float2* A = cv.take<float2>((size_t)K * C * H * P);
   float2* B = cv.take<float2>((size_t)C * S * P);
-  if (cv.overflow) return CVHRF_EWORKSPACE;
+  if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   if ((rc = launch_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
@@ -425,7 +425,7 @@ extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, co
   Carver cv(workspace, workspace_bytes);
   float2* A = cv.take<float2>((size_t)C * S * P);
   float2* B = cv.take<float2>((size_t)K * C * H * P);
-  if (cv.overflow) return CVHRF_EWORKSPACE;
+  if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   if ((rc = launch_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;

@@ -35,8 +35,8 @@ struct Carver {
     size_t off = align_up(used, 256);
     size_t bytes = count * sizeof(T);
     used = off + bytes;
-    if (used > cap || (base == nullptr && count > 0)) { overflow = true; return nullptr; }
-    return reinterpret_cast<T*>(base + off);
+    if (used > cap) { overflow = true; return nullptr; }
+    return base ? reinterpret_cast<T*>(base + off) : nullptr;  // null base: size query only
   }
 };
 

@@ -1,0 +1,322 @@
+// Complex-field tile rasterizer, forward (replaces rasterizer_splat.cu:325-548,
+// forward.cu geometry kernels and forward_splat.cu).
+//
+// Phase 1 (geometry): one fused kernel per Gaussian computes visibility, the 2D mean,
+// the 2D covariance, radius, tile count, render constants and the depth sort key;
+// a stable radix sort orders Gaussians by depth key; a scan of tile counts in that
+// order gives each Gaussian's contiguous slot range for its (tile, Gaussian) pairs.
+// Phase 2 (render): pairs are emitted in (depth, index) order and stably sorted by
+// tile, which reproduces the reference's (tile | depth) 64-bit key order exactly;
+// then one CTA per 16x16 tile composites all K planes in a single pass over the
+// tile's Gaussian list (the reference makes one pass per plane).
+#include "raster_ws.cuh"
+
+namespace cvhrf {
+
+namespace {
+
+__global__ void __launch_bounds__(256) preprocess_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= s.N) return;
+  float Wm[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) Wm[k] = __ldg(&s.view_matrix[k]);
+  const float x = s.cam_means[3 * i], y = s.cam_means[3 * i + 1], zc = s.cam_means[3 * i + 2];
+  // visibility: the intended test of checkFrustum/in_frustum (rasterizer_splat.cu:42-62,
+  // auxiliary.h:196-221) on the camera-space depth: z > 0.2 and near < z < far
+  g.vis[i] = (zc > 0.2f && zc > cam.near_plane && zc < cam.far_plane) ? 1u : 0u;
+  const float2 m2 = means2d(x, y, zc, cam);
+  float J[6], Sig[9], JW[6];
+  jacobian(x, y, zc, cam, J);
+  cov3d(s.quats + 4 * i, s.scales + 3 * i, Sig);
+  const float4 cov = cov2d(J, Wm, Sig, JW);
+  g.means2d[i] = m2;
+  g.cov2d[i] = cov;
+  // preprocessGaussiansKernel (forward_splat.cu:17-98) on z_vals
+  const float z = s.z_vals[i];
+  int radius = 0;
+  uint32_t tiles = 0;
+  if (!(z <= cam.near_plane || z >= cam.far_plane)) {
+    radius = splat_radius(cov);
+    if (radius != 0) {
+      uint2 rmin, rmax;
+      tile_rect(m2, radius, cam.grid_x, cam.grid_y, rmin, rmax);
+      tiles = (rmax.y - rmin.y) * (rmax.x - rmin.x);
+    }
+  }
+  g.radii[i] = radius;
+  g.tiles[i] = tiles;
+  g.key[i] = tiles > 0 ? depth_key(z) : 0xFFFFFFFFu;
+  g.order[i] = (uint32_t)i;
+  // render constants, computed as renderTileKernel does per pair (forward_splat.cu:200-216)
+  const float det = cov.x * cov.w - cov.y * cov.z;
+  const float det_inv = 1.0f / det;
+  g.conic[i] = make_float4(cov.w * det_inv, -cov.y * det_inv, -cov.z * det_inv, cov.x * det_inv);
+  g.rec0[i] = make_float4(m2.x, m2.y, s.opacities[i], 0.f);
+  for (int c = 0; c < s.C; ++c) {
+    float sn, cs;
+    __sincosf(s.phase[i * s.C + c], &sn, &cs);
+    const float col = s.colours[i * s.C + c];
+    g.cp[(size_t)i * s.C + c] = make_float2(col * cs, col * sn);
+  }
+}
+
+__global__ void gather_tiles_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ tiles,
+                                    uint32_t* __restrict__ out, int N) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < N) out[i] = tiles[order[i]];
+}
+
+__global__ void counts_kernel(const uint32_t* offsets, const uint32_t* vis_scan, int N, int32_t* counts) {
+  counts[0] = N > 0 ? (int32_t)offsets[N - 1] : 0;
+  counts[1] = N > 0 ? (int32_t)vis_scan[N - 1] : 0;
+}
+
+__global__ void __launch_bounds__(256) emit_pairs_kernel(GeomWs g, Camera cam, int N, BinWs b) {
+  const int si = blockIdx.x * blockDim.x + threadIdx.x;
+  if (si >= N) return;
+  const uint32_t gi = g.order[si];
+  const uint32_t n = g.tiles[gi];
+  if (n == 0) return;
+  uint32_t slot = si == 0 ? 0u : g.offsets[si - 1];
+  uint2 rmin, rmax;
+  tile_rect(g.means2d[gi], g.radii[gi], cam.grid_x, cam.grid_y, rmin, rmax);
+  for (uint32_t ty = rmin.y; ty < rmax.y; ++ty)
+    for (uint32_t tx = rmin.x; tx < rmax.x; ++tx) {
+      b.tkey[slot] = ty * (uint32_t)cam.grid_x + tx;
+      b.slot[slot] = slot;
+      b.gauss[slot] = gi;
+      ++slot;
+    }
+}
+
+__global__ void clear_ranges_kernel(int2* ranges, int T) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < T) ranges[i] = make_int2(0, 0);
+}
+
+__global__ void ranges_kernel(const uint32_t* __restrict__ tkey, const uint32_t* __restrict__ slot,
+                              const uint32_t* __restrict__ gauss, int n, int2* ranges, int32_t* point_list) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t t = tkey[i];
+  point_list[i] = (int32_t)gauss[slot[i]];
+  if (i == 0 || tkey[i - 1] != t) ranges[t].x = i;
+  if (i == n - 1 || tkey[i + 1] != t) ranges[t].y = i + 1;
+}
+
+__global__ void visible_kernel(const float* __restrict__ cam_means, const uint32_t* __restrict__ vis_scan, int N,
+                               float near_plane, float far_plane, int64_t* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const float zc = cam_means[3 * i + 2];
+  if (zc > 0.2f && zc > near_plane && zc < far_plane) out[vis_scan[i] - 1] = i;
+}
+
+// renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
+template <int K, int C>
+__global__ void __launch_bounds__(256) render_forward_kernel(
+    const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
+    const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs,
+    int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
+  __shared__ float4 s_r0[256];
+  __shared__ float4 s_cn[256];
+  __shared__ float s_w[K][256];
+  __shared__ float2 s_cp[C][256];
+  const int tile = blockIdx.x;
+  const int tx = tile % gx, ty = tile / gx;
+  const int px = tx * kTile + (threadIdx.x & 15), py = ty * kTile + (threadIdx.x >> 4);
+  const bool inside = px < W && py < H;
+  const float pxf = (float)px, pyf = (float)py;
+  const int2 range = ranges[tile];
+  const int n = range.y - range.x;
+
+  float T[K];
+  int last[K];
+  bool done[K];
+  float2 acc[K][C];
+#pragma unroll
+  for (int p = 0; p < K; ++p) {
+    T[p] = 1.0f;
+    last[p] = 0;
+    done[p] = !inside;
+#pragma unroll
+    for (int c = 0; c < C; ++c) acc[p][c] = make_float2(0.f, 0.f);
+  }
+  bool alldone = !inside;
+
+  for (int base = 0; base < n; base += 256) {
+    if (__syncthreads_and(alldone)) break;
+    const int j = base + threadIdx.x;
+    if (j < n) {
+      const int gi = point_list[range.x + j];
+      s_r0[threadIdx.x] = rec0[gi];
+      s_cn[threadIdx.x] = conic[gi];
+#pragma unroll
+      for (int p = 0; p < K; ++p) s_w[p][threadIdx.x] = plane_probs[gi * K + p];
+#pragma unroll
+      for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
+    }
+    __syncthreads();
+    const int cnt = min(256, n - base);
+    for (int jj = 0; jj < cnt && !alldone; ++jj) {
+      const float4 r0 = s_r0[jj];
+      const float2 d = {r0.x - pxf, r0.y - pyf};
+      const float4 cn = s_cn[jj];
+      const float inv00 = cn.x, inv01 = cn.y, inv10 = cn.z, inv11 = cn.w;
+      const float power = -0.5f * (d.x * (inv00 * d.x + inv10 * d.y) + d.y * (inv01 * d.x + inv11 * d.y));
+      if (power > 0.0f) continue;
+      const float og = r0.z * expf(power);
+      bool all = true;
+#pragma unroll
+      for (int p = 0; p < K; ++p) {
+        if (!done[p]) {
+          const float w = s_w[p][jj];
+          if (w >= kPlaneCutoff) {
+            const float alpha = fminf(kMaxAlpha, og * w);
+            const float test_T = T[p] * (1.0f - alpha);
+            if (test_T < 0.0001f) done[p] = true;
+            const float wt = alpha * T[p];
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              const float2 v = s_cp[c][jj];
+              acc[p][c].x = fmaf(wt, v.x, acc[p][c].x);
+              acc[p][c].y = fmaf(wt, v.y, acc[p][c].y);
+            }
+            T[p] = test_T;
+            last[p] = base + jj + 1;
+          }
+        }
+        all = all && done[p];
+      }
+      alldone = all;
+    }
+  }
+  if (!inside) return;
+  const size_t HW = (size_t)H * W, pix = (size_t)py * W + px;
+#pragma unroll
+  for (int p = 0; p < K; ++p) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) field[(p * C + c) * HW + pix] = acc[p][c];
+    final_T[p * HW + pix] = T[p];
+    n_contrib[p * HW + pix] = last[p];
+  }
+}
+
+template <int K>
+int launch_render_k(int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
+                    const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
+  switch (C) {
+    case 1: render_forward_kernel<K, 1><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 2: render_forward_kernel<K, 2><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    default: render_forward_kernel<K, 3><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+  }
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+}  // namespace
+}  // namespace cvhrf
+
+using namespace cvhrf;
+
+extern "C" size_t cvhrf_raster_geometry_workspace_bytes(int N, int K, int C) {
+  (void)K;
+  if (N < 0 || C < 1) return 0;
+  return carve_geom(nullptr, (size_t)-1, N > 0 ? N : 1, C).bytes + 256;
+}
+
+static GeomWs carve_geom_checked(void* ws, size_t bytes, int N, int C, bool& ok) {
+  GeomWs g = carve_geom(ws, bytes, N > 0 ? N : 1, C);
+  ok = g.bytes != 0 && ws != nullptr;
+  return g;
+}
+
+extern "C" int cvhrf_raster_forward_geometry(const cvhrf_raster_scene* scene, void* geom_ws, size_t geom_bytes,
+                                             int32_t* counts_dev, void* stream) {
+  if (!scene_ok(scene) || !counts_dev) return CVHRF_EINVAL;
+  const cvhrf_raster_scene& s = *scene;
+  bool ok;
+  GeomWs g = carve_geom_checked(geom_ws, geom_bytes, s.N, s.C, ok);
+  if (!ok) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Camera cam = make_camera(s);
+  const int N = s.N;
+  if (N > 0) {
+    const int nb = (N + 255) / 256;
+    preprocess_kernel<<<nb, 256, 0, st>>>(s, cam, g);
+    CVHRF_LAUNCH_CHECK();
+    int alt = 0, rc;
+    if ((rc = radix_sort_pairs(g.key, g.order, g.key_alt, g.order_alt, N, 0, 32, g.scratch, st, &alt))) return rc;
+    if (alt) {  // 4 passes of 8 bits always end in the primary buffers; kept for safety
+      CVHRF_CUDA_TRY(cudaMemcpyAsync(g.order, g.order_alt, N * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    }
+    gather_tiles_kernel<<<nb, 256, 0, st>>>(g.order, g.tiles, g.offsets, N);
+    CVHRF_LAUNCH_CHECK();
+    if ((rc = inclusive_scan_u32(g.offsets, g.offsets, N, g.scratch, st))) return rc;
+    if ((rc = inclusive_scan_u32(g.vis, g.vis, N, g.scratch, st))) return rc;
+  }
+  counts_kernel<<<1, 1, 0, st>>>(g.offsets, g.vis, N, counts_dev);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+extern "C" size_t cvhrf_raster_binning_workspace_bytes(int N, int num_pairs, int W, int H) {
+  (void)N; (void)W; (void)H;
+  if (num_pairs < 0) return 0;
+  return carve_bin(nullptr, (size_t)-1, num_pairs).bytes + 256;
+}
+
+extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
+                                           int num_pairs, int num_visible, void* bin_ws, size_t bin_bytes,
+                                           void* field, float* final_Ts, int32_t* n_contrib, int32_t* point_list,
+                                           int32_t* ranges, int64_t* visible_indices, void* stream) {
+  if (!scene_ok(scene) || num_pairs < 0 || num_visible < 0 || !field || !final_Ts || !n_contrib || !ranges)
+    return CVHRF_EINVAL;
+  if ((num_pairs > 0 && !point_list) || (num_visible > 0 && !visible_indices)) return CVHRF_EINVAL;
+  const cvhrf_raster_scene& s = *scene;
+  bool ok;
+  GeomWs g = carve_geom_checked(const_cast<void*>(geom_ws), geom_bytes, s.N, s.C, ok);
+  if (!ok) return CVHRF_EWORKSPACE;
+  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs);
+  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Camera cam = make_camera(s);
+  const int T = cam.grid_x * cam.grid_y;
+  int rc;
+  clear_ranges_kernel<<<(T + 255) / 256, 256, 0, st>>>((int2*)ranges, T);
+  CVHRF_LAUNCH_CHECK();
+  if (num_pairs > 0) {
+    emit_pairs_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(g, cam, s.N, b);
+    CVHRF_LAUNCH_CHECK();
+    int alt = 0;
+    if ((rc = radix_sort_pairs(b.tkey, b.slot, b.tkey_alt, b.slot_alt, num_pairs, 0, tile_bits(T), b.scratch, st,
+                               &alt)))
+      return rc;
+    if (alt) {  // keep the sorted result in the primary buffers (the backward reads b.slot)
+      CVHRF_CUDA_TRY(cudaMemcpyAsync(b.tkey, b.tkey_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+      CVHRF_CUDA_TRY(cudaMemcpyAsync(b.slot, b.slot_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    }
+    ranges_kernel<<<(num_pairs + 255) / 256, 256, 0, st>>>(b.tkey, b.slot, b.gauss, num_pairs, (int2*)ranges,
+                                                           point_list);
+    CVHRF_LAUNCH_CHECK();
+  }
+  if (num_visible > 0) {
+    visible_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(s.cam_means, g.vis, s.N, s.near_plane, s.far_plane,
+                                                      visible_indices);
+    CVHRF_LAUNCH_CHECK();
+  }
+  dim3 grid(T);
+  const int2* rg = (const int2*)ranges;
+  float2* f = (float2*)field;
+  switch (s.K) {
+    case 1: return launch_render_k<1>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 2: return launch_render_k<2>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 3: return launch_render_k<3>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 4: return launch_render_k<4>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 5: return launch_render_k<5>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 6: return launch_render_k<6>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 7: return launch_render_k<7>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    default: return launch_render_k<8>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+  }
+}

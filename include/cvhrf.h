@@ -104,6 +104,70 @@ int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan,
                                        void* grad_fields,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+
+/* ---- complex-field tile rasterizer ---------------------------------------- */
+/*
+ * Inputs of SplatTileCuda.forward (python_import.py:283-313), all float32 device
+ * arrays, contiguous: cam_means N x 3, z_vals N, quats N x 4, scales N x 3,
+ * colours N x C, phase N x C, opacities N, plane_probs N x K, view_matrix 3 x 3
+ * (row-major).  C <= 3 (MAX_CHANNELS), K <= 8 (MAX_PLANES); tiles are 16 x 16.
+ */
+typedef struct {
+  int N, K, C, W, H;
+  float fx, fy, px, py, near_plane, far_plane;
+  const float* cam_means;
+  const float* z_vals;
+  const float* quats;
+  const float* scales;
+  const float* colours;
+  const float* phase;
+  const float* opacities;
+  const float* plane_probs;
+  const float* view_matrix;
+} cvhrf_raster_scene;
+
+/*
+ * Forward, phase 1 (replaces rasterizer_splat.cu:363-432: markVisible, means2d,
+ * cov2d, preprocessGaussiansKernel, CUB scan): per-Gaussian projection, radius and
+ * tile count, depth-key sort, pair offsets.  Writes counts_dev[0] = number of
+ * (tile, Gaussian) pairs and counts_dev[1] = number of visible Gaussians (device
+ * int32[2]).  `geom_ws` must stay untouched until the backward has run.
+ */
+size_t cvhrf_raster_geometry_workspace_bytes(int N, int K, int C);
+int cvhrf_raster_forward_geometry(const cvhrf_raster_scene* scene, void* geom_ws, size_t geom_bytes,
+                                  int32_t* counts_dev, void* stream);
+
+/*
+ * Forward, phase 2 (replaces rasterizer_splat.cu:435-548: duplicateWithKeys, CUB
+ * radix sort, identifyTileRanges, renderTileKernel): emits and stably sorts the
+ * pairs, renders all K planes in one pass per tile.  Outputs (device):
+ *   field K x C x H x W complex64; final_Ts K x H x W f32; n_contrib K x H x W i32;
+ *   point_list num_pairs i32; ranges (tiles x 2) i32; visible_indices num_visible i64.
+ * `bin_ws` must stay untouched until the backward has run.
+ */
+size_t cvhrf_raster_binning_workspace_bytes(int N, int num_pairs, int W, int H);
+int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
+                                int num_pairs, int num_visible, void* bin_ws, size_t bin_bytes,
+                                void* field, float* final_Ts, int32_t* n_contrib, int32_t* point_list,
+                                int32_t* ranges, int64_t* visible_indices, void* stream);
+
+/*
+ * Backward (replaces rasterizer_splat.cu:551-684, renderBackwardTileKernel and the
+ * geometry backward): atomic-free — each tile writes one gradient record per
+ * (tile, Gaussian) pair, then one thread per Gaussian reduces its records and
+ * chains them through the projection.  grad_field: K x C x H x W complex64.
+ * Gradient outputs are dense N x {3,1,4,3,C,C,1,K} float32 (grad_z_vals is all 0
+ * as in the reference).
+ */
+size_t cvhrf_raster_backward_workspace_bytes(int num_pairs, int K, int C);
+int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
+                          const void* bin_ws, size_t bin_bytes, int num_pairs,
+                          const void* grad_field, const float* final_Ts, const int32_t* n_contrib,
+                          const int32_t* point_list, const int32_t* ranges, void* bwd_ws, size_t bwd_bytes,
+                          float* grad_cam_means, float* grad_z_vals, float* grad_quats, float* grad_scales,
+                          float* grad_colours, float* grad_phase, float* grad_opacities,
+                          float* grad_plane_probs, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

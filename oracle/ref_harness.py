@@ -123,6 +123,14 @@ def view_buffer(R):
     return buf[:9].view(3, 3)
 
 
+_last_info = None
+
+
+def get_rasterizer_info():
+    """forward_info (final_Ts, n_contrib, point_list, ranges, visible) of the last RefSplatTileCuda forward."""
+    return _last_info
+
+
 class RefSplatTileCuda(torch.autograd.Function):
     """python_import.py:283-342."""
 
@@ -134,7 +142,9 @@ class RefSplatTileCuda(torch.autograd.Function):
         output, info = get_rasterizer().forward(cam_means_3D, z_vals, quats, scales, colours, phase, opacities,
                                                 plane_probs, fx, fy, px, py, view_matrix, img_size, tile_size,
                                                 near_plane, far_plane)
+        global _last_info
         ctx.info = info
+        _last_info = info
         return output, info[-1]
 
     @staticmethod
