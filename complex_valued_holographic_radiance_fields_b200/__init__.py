@@ -9,5 +9,6 @@ All arithmetic runs in ``libcvhrf.so``; there is no CPU fallback.
 from .propagation import (BandlimitedPropagation, BandlimitedPropagationFunction,  # noqa: F401
                           PlanePropagationFunction, propagate, propagate_planes)
 from .rasterizer import SplatTileCuda, splat_tile_cuda  # noqa: F401,E402
+from .optimizer import SparseGaussianAdam, sparse_adam_update  # noqa: F401,E402
 
 __version__ = "0.1.0"

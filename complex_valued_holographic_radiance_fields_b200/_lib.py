@@ -38,7 +38,14 @@ SIGNATURES = {
     "cvhrf_raster_backward_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cvhrf_raster_backward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 9),
+    "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
 }
+
+
+class AdamGroup(ctypes.Structure):
+    """cvhrf_adam_group (include/cvhrf.h)."""
+    _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
+                ("N", c_int), ("D", c_int), ("dense", c_int), ("lr", c_float), ("eps", c_float)]
 
 
 class RasterScene(ctypes.Structure):

@@ -1,0 +1,74 @@
+// Fused sparse Adam over visible Gaussians (replaces conv.cu:1200-1246, sparse_adam_kernel /
+// adamUpdate, and the per-group loop of utils/optimizer.py:180-265).
+//
+// The reference launches one kernel per parameter group with a (V, B) grid of
+// D-thread blocks (3-4 threads per block) after gathering the visible gradient rows
+// into a fresh (B, V, D) tensor.  Here all groups are one launch, one thread per
+// updated element, reading the dense gradient rows in place.  Update per element
+// (no bias correction, as in the reference):
+//   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g g;  p += -lr m / (sqrt(v) + eps)
+// Dense groups (1-D parameters, optimizer.py:207-217) update every row.
+#include "common.cuh"
+
+namespace cvhrf {
+namespace {
+
+constexpr int kMaxGroups = 16;
+struct AdamLaunch {
+  int n;
+  cvhrf_adam_group g[kMaxGroups];
+  long long start[kMaxGroups + 1];  // element prefix over groups
+};
+
+__global__ void __launch_bounds__(256) sparse_adam_kernel(AdamLaunch L, const int64_t* __restrict__ visible,
+                                                          float b1, float b2) {
+  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= L.start[L.n]) return;
+  int gi = 0;
+#pragma unroll 1
+  while (gi + 1 < L.n && e >= L.start[gi + 1]) ++gi;
+  const cvhrf_adam_group& G = L.g[gi];
+  const long long local = e - L.start[gi];
+  const long long r = local / G.D;
+  const int d = (int)(local - r * G.D);
+  const long long row = G.dense ? r : visible[r];
+  const size_t idx = (size_t)row * G.D + d;
+  const float Register_param_grad = G.grad[idx];
+  float Register_exp_avg = G.exp_avg[idx];
+  float Register_exp_avg_sq = G.exp_avg_sq[idx];
+  Register_exp_avg = b1 * Register_exp_avg + (1.0f - b1) * Register_param_grad;
+  Register_exp_avg_sq = b2 * Register_exp_avg_sq + (1.0f - b2) * Register_param_grad * Register_param_grad;
+  const float step = -G.lr * Register_exp_avg / (sqrtf(Register_exp_avg_sq) + G.eps);
+  G.param[idx] += step;
+  G.exp_avg[idx] = Register_exp_avg;
+  G.exp_avg_sq[idx] = Register_exp_avg_sq;
+}
+
+}  // namespace
+}  // namespace cvhrf
+
+using namespace cvhrf;
+
+extern "C" int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, const int64_t* visible, int V, float b1,
+                                 float b2, void* stream) {
+  if (!groups || ngroups < 0 || ngroups > kMaxGroups || V < 0 || (V > 0 && !visible)) return CVHRF_EINVAL;
+  AdamLaunch L{};
+  L.n = 0;
+  long long tot = 0;
+  for (int i = 0; i < ngroups; ++i) {
+    const cvhrf_adam_group& g = groups[i];
+    if (g.D < 1 || g.N < 0 || !g.param || !g.grad || !g.exp_avg || !g.exp_avg_sq) return CVHRF_EINVAL;
+    const long long rows = g.dense ? g.N : V;
+    if (rows == 0) continue;
+    L.g[L.n] = g;
+    L.start[L.n] = tot;
+    tot += rows * g.D;
+    ++L.n;
+  }
+  L.start[L.n] = tot;
+  if (tot == 0) return CVHRF_OK;
+  const long long blocks = (tot + 255) / 256;
+  sparse_adam_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(L, visible, b1, b2);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}

@@ -1,0 +1,96 @@
+"""Sparse Adam over visible Gaussians (the ``utils/optimizer.py`` / ``adamUpdate`` surface).
+
+* ``SparseGaussianAdam(params, lr, eps)`` with ``.step(visible_chunk)`` mirrors
+  utils/optimizer.py:174-265: one tensor per param group, lazily created
+  ``exp_avg``/``exp_avg_sq``, betas fixed at 0.9/0.999, no bias correction, 1-D
+  parameters updated densely, 2-D/3-D parameters only at the visible rows.  All
+  groups are updated by ONE fused kernel launch (cvhrf_sparse_adam).
+* ``sparse_adam_update(param, grad, exp_avg, exp_avg_sq, visible_chunk, lr, b1, b2, eps)``
+  mirrors python_import.py:457-460: ``grad`` is the compacted (B, V, D) gradient of
+  the reference's adamUpdate (conv.cu:1230-1246).
+"""
+import ctypes
+
+import torch
+
+from . import _lib
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _launch(groups, visible, b1, b2, device):
+    if not groups:
+        return
+    arr = (_lib.AdamGroup * len(groups))(*groups)
+    V = 0 if visible is None else visible.numel()
+    vp = ctypes.c_void_p(visible.data_ptr()) if V > 0 else ctypes.c_void_p(0)
+    _lib.check(_lib.lib().cvhrf_sparse_adam(arr, len(groups), vp, V, float(b1), float(b2),
+                                            ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)),
+               "cvhrf_sparse_adam")
+
+
+def _group(param, grad, m, v, N, D, dense, lr, eps):
+    return _lib.AdamGroup(param.data_ptr(), grad.data_ptr(), m.data_ptr(), v.data_ptr(), int(N), int(D),
+                          int(dense), float(lr), float(eps))
+
+
+class SparseGaussianAdam(torch.optim.Adam):
+    """utils/optimizer.py:174-265."""
+
+    def __init__(self, params, lr, eps):
+        super().__init__(params=params, lr=lr, eps=eps)
+
+    @torch.no_grad()
+    def step(self, visible_chunk):
+        groups, keep = [], []
+        vis = visible_chunk.to(torch.int64).contiguous()
+        device = None
+        for group in self.param_groups:
+            assert len(group["params"]) == 1, "more than one tensor in group"
+            param = group["params"][0]
+            if param.grad is None:
+                continue
+            state = self.state[param]
+            if len(state) == 0:
+                state["step"] = torch.tensor(0.0, dtype=torch.float32)
+                state["exp_avg"] = torch.zeros_like(param, memory_format=torch.preserve_format)
+                state["exp_avg_sq"] = torch.zeros_like(param, memory_format=torch.preserve_format)
+            if vis.numel() == 0:
+                continue
+            if not (param.is_cuda and param.dtype == torch.float32 and param.is_contiguous()):
+                raise RuntimeError("SparseGaussianAdam needs contiguous float32 CUDA parameters")
+            grad = param.grad.contiguous()
+            keep.append(grad)
+            if param.dim() == 1:
+                groups.append(_group(param, grad, state["exp_avg"], state["exp_avg_sq"], param.shape[0], 1, 1,
+                                     group["lr"], group["eps"]))
+            elif param.dim() == 2:
+                groups.append(_group(param, grad, state["exp_avg"], state["exp_avg_sq"], param.shape[0],
+                                     param.shape[1], 0, group["lr"], group["eps"]))
+            elif param.dim() == 3:  # (B, N, D): one group per leading slice
+                B, N, D = param.shape
+                for b in range(B):
+                    groups.append(_group(param[b], grad[b], state["exp_avg"][b], state["exp_avg_sq"][b], N, D, 0,
+                                         group["lr"], group["eps"]))
+            else:
+                raise NotImplementedError("parameters with more than 3 dimensions")
+            device = param.device
+        if groups:
+            for i in range(0, len(groups), 16):
+                _launch(groups[i:i + 16], vis, 0.9, 0.999, device)
+
+
+def sparse_adam_update(param, grad, exp_avg, exp_avg_sq, visible_chunk, lr, b1, b2, eps):
+    """python_import.py:457-460 / conv.cu:1230-1246: param/exp_avg/exp_avg_sq (B, N, D) in place,
+    grad (B, V, D) compacted to the visible rows."""
+    B, N, D = param.shape
+    V = visible_chunk.numel()
+    vis = visible_chunk.to(torch.int64).contiguous()
+    # the kernel reads dense rows; scatter the compacted rows into a dense view
+    dense = torch.zeros_like(param)
+    if V > 0:
+        dense[:, vis] = grad.reshape(B, V, D)
+    groups = [_group(param[b], dense[b], exp_avg[b], exp_avg_sq[b], N, D, 0, lr, eps) for b in range(B)]
+    _launch(groups, vis, b1, b2, param.device)

@@ -138,7 +138,7 @@ def render_inputs(params, camera):
         params["pre_act_quats"][idxs], params["pre_act_scales"][idxs], params["pre_act_phase"][idxs],
         params["pre_act_opacities"][idxs], params["pre_act_plane_assignment"][idxs])
     cam_means = params["means"][idxs] @ R + T
-    kw = dict(cam_means_3D=cam_means, z_vals=cam_means[:, 2], quats=quats, scales=scales,
+    kw = dict(cam_means_3D=cam_means, z_vals=cam_means[:, 2].contiguous(), quats=quats, scales=scales,
               colours=params["colours"][idxs], phase=phase, opacities=opacities, plane_probs=plane_probs,
               fx=camera.fx, fy=camera.fy, px=camera.px, py=camera.py, view_matrix=R,
               img_size=(camera.W, camera.H), near_plane=camera.near, far_plane=camera.far)

@@ -168,6 +168,31 @@ int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void* geom_ws, 
                           float* grad_colours, float* grad_phase, float* grad_opacities,
                           float* grad_plane_probs, void* stream);
 
+/* ---- sparse Adam ----------------------------------------------------------- */
+/*
+ * One parameter group: param / exp_avg / exp_avg_sq / grad are dense N x D float32
+ * (device).  Sparse groups update the rows listed in `visible`; dense groups (the
+ * reference's 1-D parameters, utils/optimizer.py:207-217) update all N rows.
+ */
+typedef struct {
+  float* param;
+  const float* grad;
+  float* exp_avg;
+  float* exp_avg_sq;
+  int N, D;
+  int dense;
+  float lr, eps;
+} cvhrf_adam_group;
+
+/*
+ * All groups in one launch (replaces conv.cu:1230-1246 adamUpdate, called once per
+ * group by SparseGaussianAdam.step, utils/optimizer.py:219-253; the gathered
+ * (B, V, D) gradient copy is not needed — dense gradient rows are read in place).
+ * visible: V int64 row indices (device).  At most 16 groups.
+ */
+int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, const int64_t* visible, int V,
+                      float beta1, float beta2, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

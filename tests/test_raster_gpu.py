@@ -86,3 +86,43 @@ def test_backward_vs_reference(cuda, ref, case):
     names = ["cam_means", "quats", "scales", "colours", "phase", "opacities", "plane_probs"]
     errs = {n: rel(a, b) for n, a, b in zip(names, mine, theirs)}
     assert all(e < GRAD_TOL for e in errs.values()), errs
+
+
+ORACLE_CASES = [
+    dict(N=1500, W=100, H=75, K=3, C=3),     # edge tiles in both directions
+    dict(N=800, W=64, H=48, K=2, C=1),
+    dict(N=3000, W=200, H=136, K=4, C=2),
+]
+
+
+@pytest.mark.parametrize("case", ORACLE_CASES, ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
+def test_forward_backward_vs_oracle(cuda, case):
+    """libcvhrf vs the scalar-C restatement (oracle/raster_oracle.c), incl. edge tiles."""
+    import numpy as np
+    from oracle import raster_oracle as RO
+    kw = inputs(case["N"], case["W"], case["H"], case["K"], case["C"], seed=3)
+    field, info = RZ.rasterize_forward(*SC.splat_args(kw))
+    inp = dict(cam_means=kw["cam_means_3D"], z_vals=kw["z_vals"], quats=kw["quats"], scales=kw["scales"],
+               colours=kw["colours"], phase=kw["phase"], opacities=kw["opacities"], plane_probs=kw["plane_probs"],
+               view=kw["view_matrix"])
+    inp = {k: v.cpu().numpy() for k, v in inp.items()}
+    cam = (case["W"], case["H"], kw["fx"], kw["fy"], kw["px"], kw["py"], kw["near_plane"], kw["far_plane"])
+    f = RO.forward(inp, *cam)
+    assert np.array_equal(info["point_list"][:info["num_pairs"]].cpu().numpy(), f["point_list"])
+    assert np.array_equal(info["ranges"].cpu().numpy(), f["ranges"])
+    assert np.array_equal(info["visible"].cpu().numpy(), f["visible"])
+    assert int((info["n_contrib"].cpu().numpy() != f["n_contrib"]).sum()) == 0
+    assert rel(info["final_Ts"].cpu(), torch.from_numpy(f["final_Ts"])) < TOL
+    assert rel(field.cpu(), torch.from_numpy(f["field"].astype(np.complex64))) < TOL
+    g = torch.Generator().manual_seed(9)
+    gout = torch.complex(torch.randn(field.shape, generator=g), torch.randn(field.shape, generator=g))
+    mine = RZ.rasterize_backward(gout.cuda(), kw["cam_means_3D"], kw["z_vals"], kw["quats"], kw["scales"],
+                                 kw["colours"], kw["phase"], kw["opacities"], kw["plane_probs"], kw["view_matrix"],
+                                 info)
+    og = RO.backward(inp, *cam, gout.numpy(), f)
+    names = ["cam_means", "z_vals", "quats", "scales", "colours", "phase", "opacities", "plane_probs"]
+    for n, a in zip(names, mine):
+        if n == "z_vals":
+            assert float(a.abs().max()) == 0.0
+            continue
+        assert rel(a.cpu(), torch.from_numpy(og[n])) < TOL, n
