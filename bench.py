@@ -1,0 +1,292 @@
+"""Benchmark: training iterations/sec of the wave-optics hot path.
+
+One step = render 300k Gaussians into K=3 complex planes at 800x800 (libcvhrf
+rasterizer), propagate every (plane, channel) to the SLM with 2x padding and sum
+(libcvhrf fused FFT/ASM), L2 intensity loss against a seeded target, backward
+through both, sparse Adam over the visible Gaussians (libcvhrf fused Adam).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+
+N > 1 (launched by torch.distributed.run, one rank per GPU) is view-parallel weak
+scaling: each rank renders its own camera view of the same scene with a full
+replica, gradients are all-reduced over NCCL before Adam; `value` is the whole-job
+number of view-iterations per second.
+
+`--impl reference` times the reference's CPU implementation of the path (the
+oracle port: scalar-C rasterizer restatement on all host cores + the reference's
+pure-torch propagation on torch CPU) on rank 0, and, beside it, the reference's own
+CUDA kernels rebuilt for sm_100a on this GPU (field `reference_cuda_sm100a`).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "train iters/sec (fwd+bwd+sparse Adam) @300k Gaussians, 800x800, K=3"
+N_GAUSS, IMG, K_PLANES = 300000, 800, 3
+CONFIG = {"workload": "config3: full training step, 300k Gaussians, 800x800, K=3 planes, 3 wavelengths, "
+                      "2x-padded ASM propagation (1600^2) at 8 um, L2 intensity loss, sparse Adam",
+          "gaussians": N_GAUSS, "image": [IMG, IMG], "planes": K_PLANES, "pad": 2 * IMG,
+          "l2_policy": "inputs larger than L2 (per-step working set > 300 MB)"}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def fp32_peak_tflops(sm_mhz):
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    return props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def propagation_bytes(K, C, H, W, S):
+    """HBM bytes the three-pass fused propagation moves per forward call (the kernels as built):
+    rows: read K C H W, write K C H P; columns: read K C H P, write C S P once + (K-1) RMW of C S P;
+    inverse rows: read C S P, write C S S  (complex64 = 8 B)."""
+    P = 2 * S
+    return 8 * (K * C * H * W + 2 * K * C * H * P + C * S * P * (1 + 2 * (K - 1)) + C * S * P + C * S * S)
+
+
+def run_mine(args, world, rank, local):
+    from complex_valued_holographic_radiance_fields_b200 import _lib, scene as SC
+    from complex_valued_holographic_radiance_fields_b200.distributed import dp_step
+    from complex_valued_holographic_radiance_fields_b200.profiling import op_timing
+    from complex_valued_holographic_radiance_fields_b200.train_step import HoloTrainer
+    import math
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cam = SC.look_at_camera(IMG, IMG, 2 * math.pi * rank / max(world, 1), 0.0) if world > 1 else None
+    tr = HoloTrainer(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES, device=dev, camera=cam)
+    step = (lambda t=None: dp_step(tr, t)) if world > 1 else (lambda t=None: tr.step(t))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    L = _lib.lib()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # --- device-timed region: inputs resident in HBM ---
+    barrier()
+    launches0 = L.cvhrf_kernel_launch_count()
+    sampler = ClockSampler(local)
+    with sampler, op_timing() as ops:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            loss = step()
+        t1.record()
+        barrier()
+    launches = L.cvhrf_kernel_launch_count() - launches0
+    ms = t0.elapsed_time(t1) / args.steps
+    opsum = ops.summary()
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # --- end to end: target H2D from pinned host memory + loss D2H every step ---
+    host_tgt = tr.target.cpu().pin_memory()
+    dev_tgt = torch.empty_like(tr.target)
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        dev_tgt.copy_(host_tgt, non_blocking=True)
+        float(step(dev_tgt).item())
+    e1.record()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_ms.item())
+
+    if rank != 0:
+        return None
+    clocks = sampler.summary()
+    hbm, hbm_src = peaks()
+    # roofline of the dominant operator
+    dom = max(opsum.items(), key=lambda kv: kv[1][1])
+    prop_ms = opsum.get("propagation_forward", (1, float("nan")))[1]
+    pbytes = propagation_bytes(K_PLANES, 3, IMG, IMG, IMG)
+    roof_prop = {"op": "propagation_forward (3 fused FFT/ASM kernels)", "bound": "hbm",
+                 "achieved": pbytes / (prop_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                 "peak_source": hbm_src, "algorithmic_bytes": pbytes, "traffic": None}
+    roof_prop["frac"] = roof_prop["achieved"] / hbm
+    line = {
+        "metric": METRIC, "value": world * 1000.0 / ms_max, "unit": "iters/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded, config-3 shapes)",
+        "config": dict(CONFIG, parallelism=f"view-dp{world}" if world > 1 else "single"),
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "iters/s",
+                "h2d_bytes_per_step": host_tgt.numel() * 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": int(launches),
+        "ops_ms": {k: round(v[1], 4) for k, v in opsum.items()},
+        "dominant_op": dom[0],
+        "roofline": roof_prop,
+        "clocks": clocks,
+        "loss": float(loss.item()),
+    }
+    return line
+
+
+def cpu_baseline(samples=1):
+    from oracle.cpu_step import CpuHoloStep, num_threads
+    st = CpuHoloStep(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES)
+    ts = []
+    for _ in range(samples):
+        t = time.perf_counter()
+        st.step()
+        ts.append(time.perf_counter() - t)
+    v = 1.0 / statistics.median(ts)
+    return {"value": v, "unit": "iters/s", "cores": num_threads(), "kind": "port",
+            "sample": f"{samples} full config-3 step(s) on the host: oracle/raster_oracle.c (OpenMP) rasterizer "
+                      "fwd/bwd + the reference's pure-torch propagation (python_function.py:35-78) on torch CPU + "
+                      "torch Adam"}
+
+
+def ref_cuda_step_rate(steps, warmup):
+    """The reference's own kernels (oracle/_ref, sm_100a rebuild) on this GPU, same step."""
+    from oracle import ref_harness
+    if not ref_harness.available():
+        return {"unavailable": "oracle/_ref not built"}
+    from oracle.ref_step import RefGpuHoloStep
+    from complex_valued_holographic_radiance_fields_b200.train_step import HoloTrainer
+    tr = HoloTrainer(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES, device="cuda")
+    rs = RefGpuHoloStep(tr)
+    for _ in range(warmup):
+        rs.step()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        rs.step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"value": 1000.0 / ms, "unit": "iters/s", "ms_per_step": ms,
+            "what": "reference CUDA kernels (cov3d_cuda + cuda_modules, rebuilt sm_100a) + cuFFT, same step"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    base = cpu_baseline(samples=max(1, min(args.steps, 3)))
+    line = {"metric": METRIC, "value": base["value"], "unit": "iters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded, config-3 shapes)",
+            "config": dict(CONFIG, parallelism="host cpu"), "impl": "reference", "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if torch.cuda.is_available():
+        try:
+            line["reference_cuda_sm100a"] = ref_cuda_step_rate(min(args.steps, 10), min(args.warmup, 3))
+        except Exception as e:  # the CPU number above stands on its own
+            line["reference_cuda_sm100a"] = {"unavailable": repr(e)[:200]}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    try:
+        if args.impl == "reference":
+            line = run_reference(args, world, rank)
+        else:
+            line = run_mine(args, world, rank, local)
+            if line is not None and world == 1 and not args.no_cpu_baseline:
+                line["cpu_baseline"] = cpu_baseline(samples=1)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -20,6 +20,7 @@ SIGNATURES = {
     "cvhrf_status_string": (ctypes.c_char_p, [c_int]),
     "cvhrf_last_cuda_error": (c_int, []),
     "cvhrf_version": (c_int, []),
+    "cvhrf_kernel_launch_count": (ctypes.c_ulonglong, []),
     "cvhrf_asm_plan_create": (c_int, [c_int, ctypes.POINTER(c_void_p)]),
     "cvhrf_asm_plan_destroy": (c_int, [c_void_p]),
     "cvhrf_asm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int, c_int]),

@@ -9,6 +9,8 @@ namespace cvhrf {
 
 // Records the failing cudaError_t for cvhrf_last_cuda_error() (defined in capi.cu).
 void set_last_cuda_error(int err);
+// Adds n to the process-wide count of kernels this library has launched (capi.cu).
+void count_launch(int n);
 
 #define CVHRF_CUDA_TRY(expr)                                    \
   do {                                                          \
@@ -19,7 +21,11 @@ void set_last_cuda_error(int err);
     }                                                           \
   } while (0)
 
-#define CVHRF_LAUNCH_CHECK() CVHRF_CUDA_TRY(cudaGetLastError())
+#define CVHRF_LAUNCH_CHECK()        \
+  do {                              \
+    ::cvhrf::count_launch(1);       \
+    CVHRF_CUDA_TRY(cudaGetLastError()); \
+  } while (0)
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -181,6 +181,7 @@ int inclusive_scan_u32(const uint32_t* in, uint32_t* out, int n, uint32_t* scrat
   scan_reduce_kernel<<<nb, kScanThreads, 0, st>>>(in, n, scratch);
   scan_sums_kernel<<<1, 1024, 0, st>>>(scratch, nb);
   scan_apply_kernel<<<nb, kScanThreads, 0, st>>>(in, out, n, scratch);
+  count_launch(2);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
@@ -203,6 +204,7 @@ int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int
     const int bits = min(kSortBits, end_bit - b);
     const int radix = 1 << bits;
     radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, n, b, radix, hist, nb);
+    count_launch(1);
     int rc = inclusive_scan_u32(hist, hist, radix * nb, sscr, st);
     if (rc) return rc;
     radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, ko, vo, n, b, radix, hist, nb);

@@ -1,0 +1,44 @@
+"""Data parallelism over camera views (one process per GPU, torch.distributed/NCCL).
+
+Each rank renders and back-propagates its own view against a full replica of the
+Gaussians.  Before the sparse Adam step the ranks exchange exactly two things:
+
+* the dense per-Gaussian gradients, flattened into ONE buffer and summed with a
+  single all-reduce (17 + K floats per Gaussian: means 3, scales 3, quats 4,
+  colours C, phase C, opacity 1, plane logits K);
+* the set of rows any rank saw (a uint8 mask, all-reduce MAX).
+
+Every rank then applies the identical Adam update, so replicas stay bit-identical.
+The reference has no multi-GPU path; this is the view-parallel design of its
+training loop (train.py:230-324 runs one view per iteration).
+"""
+import torch
+import torch.distributed as dist
+
+
+def allreduce_gradients_and_visibility(params, visible_rows, n_rows, group=None):
+    """Sum .grad of every tensor in `params` (dict) across ranks; return the union of visible rows."""
+    grads = [p.grad for p in params.values()]
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    mask = torch.zeros(n_rows, dtype=torch.uint8, device=flat.device)
+    mask[visible_rows] = 1
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=group)
+    off = 0
+    for p, g in zip(params.values(), grads):
+        n = g.numel()
+        p.grad = flat[off:off + n].view_as(g)
+        off += n
+    return torch.nonzero(mask, as_tuple=False).squeeze(1)
+
+
+def dp_step(trainer, target=None, group=None):
+    """One view-parallel training iteration on `trainer` (a HoloTrainer)."""
+    for p in trainer.params.values():
+        p.grad = None
+    loss, visible = trainer.forward(target)
+    loss.backward()
+    n = trainer.params["means"].shape[0]
+    visible = allreduce_gradients_and_visibility(trainer.params, visible, n, group)
+    trainer.opt.step(visible)
+    return loss.detach()

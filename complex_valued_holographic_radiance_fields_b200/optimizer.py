@@ -14,6 +14,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .profiling import timed
 
 
 def _stream(t):
@@ -78,8 +79,9 @@ class SparseGaussianAdam(torch.optim.Adam):
                 raise NotImplementedError("parameters with more than 3 dimensions")
             device = param.device
         if groups:
-            for i in range(0, len(groups), 16):
-                _launch(groups[i:i + 16], vis, 0.9, 0.999, device)
+            with timed("sparse_adam"):
+                for i in range(0, len(groups), 16):
+                    _launch(groups[i:i + 16], vis, 0.9, 0.999, device)
 
 
 def sparse_adam_update(param, grad, exp_avg, exp_avg_sq, visible_chunk, lr, b1, b2, eps):

@@ -20,6 +20,7 @@ import threading
 import torch
 
 from . import _lib
+from .profiling import timed
 
 _plans = {}
 _plans_lock = threading.Lock()
@@ -136,7 +137,8 @@ class PlanePropagationFunction(torch.autograd.Function):
         holo = torch.empty((C, S, S), dtype=torch.complex64, device=fields.device)
         ws = _workspace(S, K * C, H, C, S, fields.device)
         L = _lib.lib()
-        st = L.cvhrf_asm_propagate_planes(get_plan(S, fields.device), ctypes.c_void_p(fields.data_ptr()), K, C, H,
+        with timed("propagation_forward"):
+            st = L.cvhrf_asm_propagate_planes(get_plan(S, fields.device), ctypes.c_void_p(fields.data_ptr()), K, C, H,
                                           W, _lib.float_array(wl), _lib.float_array(ds), ctx.cfg[2], ctx.cfg[4],
                                           ctypes.c_void_p(holo.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
                                           ws.numel(), _stream(fields))
@@ -150,7 +152,8 @@ class PlanePropagationFunction(torch.autograd.Function):
         grad_fields = torch.empty((K, C, H, W), dtype=torch.complex64, device=g.device)
         ws = _workspace(S, C, S, K * C, H, g.device)
         L = _lib.lib()
-        st = L.cvhrf_asm_propagate_planes_adjoint(get_plan(S, g.device), ctypes.c_void_p(g.data_ptr()), K, C, H, W,
+        with timed("propagation_backward"):
+            st = L.cvhrf_asm_propagate_planes_adjoint(get_plan(S, g.device), ctypes.c_void_p(g.data_ptr()), K, C, H, W,
                                                   _lib.float_array(wl), _lib.float_array(ds), pitch, ap,
                                                   ctypes.c_void_p(grad_fields.data_ptr()),
                                                   ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(g))

@@ -18,6 +18,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .profiling import timed
 
 _F32 = torch.float32
 
@@ -72,8 +73,9 @@ def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_s
     gbytes = L.cvhrf_raster_geometry_workspace_bytes(N, K, C)
     geom = torch.empty(gbytes, dtype=torch.uint8, device=dev)
     counts = torch.empty(2, dtype=torch.int32, device=dev)
-    _lib.check(L.cvhrf_raster_forward_geometry(ctypes.byref(sc), _p(geom), gbytes, _p(counts), st),
-               "cvhrf_raster_forward_geometry")
+    with timed("raster_geometry"):
+        _lib.check(L.cvhrf_raster_forward_geometry(ctypes.byref(sc), _p(geom), gbytes, _p(counts), st),
+                   "cvhrf_raster_forward_geometry")
     num_pairs, num_visible = (int(v) for v in counts.cpu().tolist())  # one host sync (the reference has four)
     bbytes = L.cvhrf_raster_binning_workspace_bytes(N, num_pairs, W, H)
     binws = torch.empty(bbytes, dtype=torch.uint8, device=dev)
@@ -84,9 +86,10 @@ def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_s
     point_list = torch.zeros(max(num_pairs, 1), dtype=torch.int32, device=dev)
     ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
     vis = torch.empty(num_visible if num_pairs > 0 else 0, dtype=torch.int64, device=dev)
-    _lib.check(L.cvhrf_raster_forward_render(ctypes.byref(sc), _p(geom), gbytes, num_pairs, vis.numel(), _p(binws),
-                                             bbytes, _p(field), _p(final_Ts), _p(n_contrib), _p(point_list),
-                                             _p(ranges), _p(vis), st), "cvhrf_raster_forward_render")
+    with timed("raster_render"):
+        _lib.check(L.cvhrf_raster_forward_render(ctypes.byref(sc), _p(geom), gbytes, num_pairs, vis.numel(), _p(binws),
+                                                 bbytes, _p(field), _p(final_Ts), _p(n_contrib), _p(point_list),
+                                                 _p(ranges), _p(vis), st), "cvhrf_raster_forward_render")
     info = dict(geom=geom, gbytes=gbytes, binws=binws, bbytes=bbytes, num_pairs=num_pairs, final_Ts=final_Ts,
                 n_contrib=n_contrib, point_list=point_list, ranges=ranges, visible=vis, img=(W, H),
                 cam=(fx, fy, px, py, near, far))
@@ -116,11 +119,13 @@ def rasterize_backward(grad_field, cam, z, q, s, col, ph, op, pp, view, info):
     gph = torch.empty((N, C), dtype=_F32, device=dev)
     gop = torch.empty((N,), dtype=_F32, device=dev)
     gpp = torch.empty((N, K), dtype=_F32, device=dev)
-    _lib.check(L.cvhrf_raster_backward(ctypes.byref(sc), _p(info["geom"]), info["gbytes"], _p(info["binws"]),
-                                       info["bbytes"], npairs, _p(g), _p(info["final_Ts"]), _p(info["n_contrib"]),
-                                       _p(info["point_list"]), _p(info["ranges"]), _p(rws), rbytes, _p(gcam), _p(gz),
-                                       _p(gq), _p(gs), _p(gcol), _p(gph), _p(gop), _p(gpp), _stream(dev)),
-               "cvhrf_raster_backward")
+    with timed("raster_backward"):
+        _lib.check(L.cvhrf_raster_backward(ctypes.byref(sc), _p(info["geom"]), info["gbytes"], _p(info["binws"]),
+                                           info["bbytes"], npairs, _p(g), _p(info["final_Ts"]),
+                                           _p(info["n_contrib"]), _p(info["point_list"]), _p(info["ranges"]), _p(rws),
+                                           rbytes, _p(gcam), _p(gz), _p(gq), _p(gs), _p(gcol), _p(gph), _p(gop),
+                                           _p(gpp), _stream(dev)),
+                   "cvhrf_raster_backward")
     return gcam, gz, gq, gs, gcol, gph, gop, gpp
 
 

@@ -1,0 +1,68 @@
+"""One training iteration of the hot path (train.py:230-324 restated).
+
+    render (model.py:1365-1416)   -> splat_tile_cuda           (libcvhrf rasterizer)
+    per-plane propagation + sum   -> propagate_planes          (libcvhrf fused FFT/ASM)
+    loss = mean((|holo|^2 - target)^2)                          (torch, elementwise)
+    backward                      -> libcvhrf adjoints
+    SparseGaussianAdam.step(visible)                            (libcvhrf fused Adam)
+
+Optics follow train.py:839-865 with the config's overrides: wavelengths 639/532/473 nm,
+planes at linspace(-V/2, V/2, K) + d_val (V = 4 mm, d_val = -2 mm -> -4, -2, 0 mm for
+K = 3), each plane propagated by -d_p (model.py:1259), pad_size = aperture = max(W, H),
+pixel pitch 8 um (the config's value; the script default is 3.74 um).
+
+The reference optimizer receives the rasterizer's ``visible_indices``, which index the
+depth-sorted subset, not the parameter rows; here they are mapped back through the
+sort permutation (``idxs[visible]``) so the update lands on the rows that were seen.
+"""
+import torch
+
+from . import scene as SC
+from .optimizer import SparseGaussianAdam
+from .propagation import propagate_planes
+from .rasterizer import splat_tile_cuda
+
+WAVELENGTHS = [639e-9, 532e-9, 473e-9]
+
+
+def plane_distances(K, volume_depth=4e-3, d_val=-2e-3):
+    if K == 1:
+        return torch.tensor([d_val], dtype=torch.float32)
+    return torch.linspace(-volume_depth / 2.0, volume_depth / 2.0, K) + d_val
+
+
+class HoloTrainer:
+    def __init__(self, N=300000, W=800, H=800, K=3, pitch=8e-6, lr=1e-3, eps=1e-15, seed=0, device="cuda",
+                 camera=None, wavelengths=None, target=None):
+        self.device = torch.device(device)
+        self.W, self.H, self.K = W, H, K
+        self.S = max(W, H)
+        self.aperture = float(self.S)
+        self.pitch = pitch
+        self.wavelengths = list(wavelengths or WAVELENGTHS)
+        d = plane_distances(K)
+        self.prop_distances = [float(-d[p]) for p in range(K)]
+        self.camera = camera or SC.PinholeCamera(W, H)
+        self.params = {k: v.requires_grad_(True) for k, v in
+                       SC.make_gaussians(N, K=K, C=len(self.wavelengths), seed=seed, device=self.device).items()}
+        self.opt = SparseGaussianAdam([{"params": [p], "lr": lr} for p in self.params.values()], lr=lr, eps=eps)
+        if target is None:
+            g = torch.Generator().manual_seed(1)
+            target = torch.rand(len(self.wavelengths), self.S, self.S, generator=g)
+        self.target = target.to(self.device)
+
+    def forward(self, target=None):
+        kw, idxs = SC.render_inputs(self.params, self.camera)
+        field, visible = splat_tile_cuda(*SC.splat_args(kw))
+        holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
+        tgt = self.target if target is None else target
+        loss = ((holo.real.square() + holo.imag.square() - tgt) ** 2).mean()
+        return loss, idxs[visible]
+
+    def step(self, target=None):
+        for p in self.params.values():
+            p.grad = None
+        loss, visible = self.forward(target)
+        loss.backward()
+        self.opt.step(visible)
+        return loss.detach()

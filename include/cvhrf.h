@@ -43,6 +43,9 @@ const char* cvhrf_status_string(int status);
 int cvhrf_last_cuda_error(void);
 /* Library version, e.g. 100 for 0.1.0. */
 int cvhrf_version(void);
+/* Number of CUDA kernels this library has launched in this process (diagnostics;
+ * no counterpart in the reference). */
+unsigned long long cvhrf_kernel_launch_count(void);
 
 /* ---- band-limited angular-spectrum propagation ---------------------------- */
 /*

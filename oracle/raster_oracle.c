@@ -3,7 +3,7 @@
  *
  * TEST INFRASTRUCTURE ONLY: the checker for libcvhrf's rasterizer kernels and the
  * timed CPU baseline of bench.py.  Scalar C, one thread, float32 arithmetic with no
- * FMA contraction (built with -ffp-contract=off), so values agree with the GPU to
+ * FMA contraction (built with -ffp-contract=off); tile loops run on OpenMP threads, so values agree with the GPU to
  * rounding, not bit for bit; integer outputs (pair list, ranges) agree exactly
  * unless a radius or tile bound lands within one ulp of an integer.
  *
@@ -26,6 +26,9 @@
  *                 (cov2d / Jacobian / cov3d / means2d backward)
  */
 #include <math.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -165,6 +168,7 @@ int ora_raster_forward(int N, int K, int C, int W, int H, float fx, float fy, fl
   float* cv = (float*)malloc(sizeof(float) * 4 * (N + 1));
   int* rad = (int*)malloc(sizeof(int) * (N + 1));
   long total = 0;
+#pragma omp parallel for reduction(+ : total) schedule(static)
   for (int i = 0; i < N; ++i) {
     const float zc = cam[3 * i + 2];
     visible[i] = (zc > 0.2f && zc > near_plane && zc < far_plane);
@@ -211,6 +215,7 @@ int ora_raster_forward(int N, int K, int C, int W, int H, float fx, float fy, fl
   const size_t HW = (size_t)H * W;
   for (size_t i = 0; i < (size_t)K * C * HW * 2; ++i) field[i] = 0.f;
   for (size_t i = 0; i < (size_t)K * HW; ++i) { final_T[i] = 1.f; n_contrib[i] = 0; }
+#pragma omp parallel for schedule(dynamic, 4)
   for (int t = 0; t < T; ++t) {
     const int a = ranges[2 * t], b = ranges[2 * t + 1];
     if (b <= a) continue;
@@ -271,6 +276,7 @@ void ora_raster_backward(int N, int K, int C, int W, int H, float fx, float fy, 
   float* cv = (float*)malloc(sizeof(float) * 4 * (N + 1));
   float* gm = (float*)calloc(2 * (size_t)N + 2, sizeof(float));
   float* gc = (float*)calloc(4 * (size_t)N + 4, sizeof(float));
+#pragma omp parallel for schedule(static)
   for (int i = 0; i < N; ++i) {
     float J[6], Sig[9], JW[6];
     means2d(&s, i, m2 + 2 * i);
@@ -282,6 +288,7 @@ void ora_raster_backward(int N, int K, int C, int W, int H, float fx, float fy, 
   memset(g_op, 0, sizeof(float) * N);
   memset(g_pl, 0, sizeof(float) * N * K);
   const size_t HW = (size_t)H * W;
+#pragma omp parallel for schedule(dynamic, 4)
   for (int t = 0; t < T; ++t) {
     const int a = ranges[2 * t], b = ranges[2 * t + 1];
     if (b <= a) continue;
@@ -322,27 +329,41 @@ void ora_raster_backward(int N, int K, int C, int W, int H, float fx, float fy, 
               const float dre = grad_field[2 * ((p * C + c) * HW + pix)], dim = grad_field[2 * ((p * C + c) * HW + pix) + 1];
               dL_dalpha += (cr - acc_re[c]) * dre;
               dL_dalpha += (ci - acc_im[c]) * dim;
+              #pragma omp atomic
               g_col[g * C + c] += dcd * (cs * dre + sn * dim);
+              #pragma omp atomic
               g_ph[g * C + c] += dcd * col * (-sn * dre + cs * dim);
             }
             dL_dalpha *= Tr;
             last_alpha = alpha;
             const float dL_dG = opac[g] * pp * dL_dalpha;
             const float gdx = G * dx, gdy = G * dy;
+            #pragma omp atomic
             gm[2 * g] += dL_dG * (-gdx * cx - gdy * cy) * (0.5f * W);
+            #pragma omp atomic
             gm[2 * g + 1] += dL_dG * (-gdy * cz - gdx * cy) * (0.5f * H);
             const float dcx = -0.5f * gdx * dx * dL_dG, dcy = -0.5f * gdx * dy * dL_dG, dcz = -0.5f * gdy * dy * dL_dG;
             const float xx = dcx * (c4[3] * di * di) * c4[3] + dcz * (-c4[1] * di * di) * (-c4[1]);
             const float xy = dcx * (c4[3] * di * di) * (-c4[1]) + dcy * (-di) + dcz * (-c4[1] * di * di) * c4[0];
             const float yy = dcx * (-c4[1] * di * di) * (-c4[1]) + dcz * (c4[0] * di * di) * c4[0];
-            gc[4 * g] += xx; gc[4 * g + 1] += xy; gc[4 * g + 2] += xy; gc[4 * g + 3] += yy;
+            #pragma omp atomic
+            gc[4 * g] += xx;
+            #pragma omp atomic
+            gc[4 * g + 1] += xy;
+            #pragma omp atomic
+            gc[4 * g + 2] += xy;
+            #pragma omp atomic
+            gc[4 * g + 3] += yy;
+            #pragma omp atomic
             g_op[g] += G * pp * dL_dalpha;
+            #pragma omp atomic
             g_pl[g * K + p] += opac[g] * G * dL_dalpha;
           }
         }
       }
   }
   /* geometry backward (backward.cu:363-497, backward_splat.cu:364-417) */
+#pragma omp parallel for schedule(static)
   for (int i = 0; i < N; ++i) {
     const float x = cam[3 * i], y = cam[3 * i + 1], zz = cam[3 * i + 2];
     float J[6], Sig[9], JW[6], c4[4];
@@ -402,6 +423,14 @@ void ora_raster_backward(int N, int K, int C, int W, int H, float fx, float fy, 
     }
   }
   free(m2); free(cv); free(gm); free(gc);
+}
+
+int ora_num_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
 }
 
 /* Fused sparse Adam restatement (conv.cu:1200-1228): rows `visible`, grad dense. */

@@ -1,0 +1,46 @@
+"""CPU (gloo, world_size 2): the view-parallel gradient exchange used before sparse Adam."""
+import os
+import socket
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from complex_valued_holographic_radiance_fields_b200.distributed import allreduce_gradients_and_visibility
+    torch.manual_seed(rank)
+    params = {"a": torch.zeros(6, 3, requires_grad=True), "b": torch.zeros(6, requires_grad=True)}
+    params["a"].grad = torch.full((6, 3), float(rank + 1))
+    params["b"].grad = torch.arange(6, dtype=torch.float32) * (rank + 1)
+    vis = torch.tensor([rank, 4]) if rank == 0 else torch.tensor([2, 4])
+    u = allreduce_gradients_and_visibility(params, vis, 6)
+    q.put((rank, params["a"].grad.tolist(), params["b"].grad.tolist(), u.tolist()))
+    dist.destroy_process_group()
+
+
+def test_allreduce_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, a, b, u in res:
+        assert a == [[3.0] * 3] * 6
+        assert b == [float(3 * i) for i in range(6)]
+        assert u == [0, 2, 4]

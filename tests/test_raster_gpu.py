@@ -40,9 +40,14 @@ CASES = [
     dict(N=2000, W=128, H=96, K=3, C=3),
     dict(N=20000, W=256, H=256, K=3, C=3),
     dict(N=5000, W=160, H=128, K=1, C=1),
-    dict(N=5000, W=144, H=112, K=5, C=2),
+    dict(N=5000, W=144, H=112, K=5, C=3),
+    dict(N=4000, W=128, H=128, K=8, C=1),
     dict(N=100000, W=800, H=800, K=3, C=3),   # config 2
 ]
+# C = 2 is not compared with the reference: it dispatches renderTileKernel<MAX_CHANNELS=3>
+# for two channels (forward_splat.cu:380-402), whose third-channel store (:263-268) lands
+# in the next plane's first channel and, for the last plane, past the end of the output.
+# C = 2 is covered against the oracle below.
 
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
@@ -61,7 +66,7 @@ def test_forward_vs_reference(cuda, ref, case):
     assert rel(field, rfield) < TOL
 
 
-@pytest.mark.parametrize("case", CASES[:4], ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
+@pytest.mark.parametrize("case", CASES[:5], ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
 def test_backward_vs_reference(cuda, ref, case):
     kw = inputs(case["N"], case["W"], case["H"], case["K"], case["C"], seed=1)
     g = torch.Generator().manual_seed(5)
