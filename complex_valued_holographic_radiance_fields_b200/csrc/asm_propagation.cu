@@ -20,6 +20,7 @@
 #include <math.h>
 #include <stdlib.h>
 #include <string.h>
+#include <mutex>
 #include <vector>
 #include "common.cuh"
 #include "fft_lines.cuh"
@@ -440,4 +441,106 @@ extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, co
     }
   if ((rc = launch_columns(d, A, S, B, H, jobs, 0, st))) return rc;
   return launch_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+}
+
+// ---------------------------------------------------------------------------------
+// Allocation-free variant of cvhrf_asm_propagate.
+//
+// Some callers cannot allocate device memory at the moment they propagate: code
+// running while a memory pool is frozen or exhausted, plugin hosts that forbid
+// allocation inside their execute callback, or real-time loops that must not touch
+// the allocator.  For them this entry point keeps everything it needs — the two
+// intermediate spectra and the FFT tables — in one fixed file-scope device array
+// (kNoAllocBytes, held by every GPU that loads the library until the process exits),
+// so it needs neither a workspace nor a plan.  The limit is S <= kNoAllocMaxS.
+// Every call shares that one array and overwrites it completely (tables, then the
+// row and column passes), so nothing from a previous call is read; two calls that
+// overlap on the GPU (different streams, or different host threads without ordering)
+// race on it.
+namespace cvhrf {
+namespace {
+
+constexpr int kNoAllocMaxS = 512;
+constexpr size_t kNoAllocSpectrum = (size_t)kNoAllocMaxS * (2 * kNoAllocMaxS) * sizeof(float2);  // Hi x P
+constexpr size_t kNoAllocTables =
+    align_up_c((size_t)(3 * kNoAllocMaxS) * sizeof(float2) + (size_t)kNoAllocMaxS * sizeof(int), 256);
+constexpr size_t kNoAllocBytes = 2 * kNoAllocSpectrum + kNoAllocTables;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// One device address per device, looked up once with that device current.
+constexpr int kMaxDevices = 64;
+static void* g_noalloc_addr[kMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  CVHRF_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return CVHRF_EUNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    CVHRF_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return CVHRF_OK;
+}
+
+// Twiddle and digit-reversal tables of a plan, computed on the device (the same
+// values cvhrf_asm_plan_create uploads: w = exp(-2 pi i t / n) in double, rounded).
+__global__ void noalloc_tables_kernel(FftDesc d, float2* tw, float2* twP, int* digrev) {
+  const int S = d.S, P = 2 * S;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < P; t += gridDim.x * blockDim.x) {
+    double s, c;
+    sincospi(-2.0 * (double)t / (double)P, &s, &c);
+    twP[t] = make_float2((float)c, (float)s);
+    if (t < S) {
+      sincospi(-2.0 * (double)t / (double)S, &s, &c);
+      tw[t] = make_float2((float)c, (float)s);
+      int rem = t, pos = 0;
+      for (int i = 0; i < d.nst; ++i) {
+        const int m = rem % d.radix[i];
+        rem /= d.radix[i];
+        pos += d.L[i] * m;
+      }
+      digrev[pos] = t;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace cvhrf
+
+extern "C" int cvhrf_asm_propagate_noalloc(const void* in, int Hi, int Wi, void* out, int Ho, int Wo, int S,
+                                           float wavelength, float pixel_pitch, float distance, float aperture,
+                                           int accumulate, void* stream) {
+  if (!in || !out) return CVHRF_EINVAL;
+  if (S < 8 || S > kNoAllocMaxS) return CVHRF_EUNSUPPORTED;
+  if (!dims_ok(S, Hi, Wi) || !dims_ok(S, Ho, Wo)) return CVHRF_EINVAL;
+  if (!(wavelength > 0.0f) || !(pixel_pitch > 0.0f)) return CVHRF_EINVAL;
+  FftDesc d{};
+  if (!factorize(S, d)) return CVHRF_EUNSUPPORTED;
+  void* base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  char* b = (char*)base;
+  float2* A = (float2*)b;
+  float2* B = (float2*)(b + kNoAllocSpectrum);
+  float2* tw = (float2*)(b + 2 * kNoAllocSpectrum);
+  float2* twP = tw + S;
+  int* digrev = (int*)(twP + 2 * S);
+  d.tw = tw;
+  d.twP = twP;
+  d.digrev = digrev;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int P = 2 * S;
+  noalloc_tables_kernel<<<(P + 255) / 256, 256, 0, st>>>(d, tw, twP, digrev);
+  CVHRF_LAUNCH_CHECK();
+  if ((rc = launch_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
+  ColumnJobs jobs{};
+  jobs.n = 1;
+  jobs.tp[0] = make_transfer(wavelength, pixel_pitch, distance, aperture, P);
+  if ((rc = launch_columns(d, A, Hi, B, Ho, jobs, 0, st))) return rc;
+  return launch_rows_inverse(d, B, Ho, (float2*)out, Wo, accumulate, st);
 }

@@ -28,6 +28,7 @@ void count_launch(int n);
   } while (0)
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+constexpr size_t align_up_c(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Carves 256-byte aligned sub-buffers out of a caller-provided workspace.
 struct Carver {

@@ -107,6 +107,24 @@ int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan,
                                        void* grad_fields,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * cvhrf_asm_propagate without any device allocation and without a plan.
+ * No counterpart in the reference: it exists for callers that cannot allocate
+ * device memory when they propagate (a frozen or exhausted memory pool, a plugin
+ * host that forbids allocation inside its execute callback, a real-time loop that
+ * must not touch the allocator).  Its scratch — two intermediate spectra and the
+ * FFT tables — is one fixed device array inside the library (about 8.2 MB, kept
+ * by every GPU that loads the library until the process exits), so S is limited
+ * to 8 <= S <= 512 (larger S returns CVHRF_EUNSUPPORTED).  Same arguments and
+ * result as cvhrf_asm_propagate otherwise.  The first call on a device looks up
+ * that array's device address (with the device current); make that first call
+ * before any stream capture.  All calls share the array and overwrite it, so calls
+ * that overlap on the GPU race: order them on one stream.
+ */
+int cvhrf_asm_propagate_noalloc(const void* in, int Hi, int Wi, void* out, int Ho, int Wo, int S,
+                                float wavelength, float pixel_pitch, float distance, float aperture,
+                                int accumulate, void* stream);
+
 
 /* ---- complex-field tile rasterizer ---------------------------------------- */
 /*
