@@ -60,6 +60,18 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[kRedV]) {
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
+// Per-Gaussian constants of the backward pixel loop, computed once per batch with the
+// reference's expressions (backward_splat.cu:194-206, 283-292), so the per-pixel
+// arithmetic is unchanged; plus a conservative bounding box of the region where
+// alpha >= 1/255 can hold (outside it the reference `continue`s, :218).
+struct BwdG {
+  float mx, my, opacity, ex;      // mean, opacity, box half-width
+  float cx, cy, cz, ey;           // conic_x, conic_y, conic_z, box half-height
+  float A, B, Cc, D;              // d cov / d conic coefficients
+  float E, G;                     // (A..G: see render_backward_kernel)
+  int ok;                         // det != 0 and the box is non-empty
+};
+
 template <int KG, int C>
 __global__ void __launch_bounds__(256) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
@@ -70,8 +82,7 @@ __global__ void __launch_bounds__(256) render_backward_kernel(
   constexpr int NW = 8;
   static_assert(6 + KG + 2 * C <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[256];
-  __shared__ float4 s_r0[256];
-  __shared__ float4 s_cov[256];
+  __shared__ BwdG s_g[256];
   __shared__ float s_w[KG][256];
   __shared__ float s_col[C][256];
   __shared__ float2 s_cs[C][256];
@@ -93,12 +104,14 @@ __global__ void __launch_bounds__(256) render_backward_kernel(
   float T[KG], last_alpha[KG];
   int last[KG];
   float2 dL[KG][C], acc_rec[KG][C], last_col[KG][C];
+  int max_last = 0;
 #pragma unroll
   for (int kk = 0; kk < KG; ++kk) {
     const int p = p0 + kk;
     const bool pv = inside && p < K;
     T[kk] = pv ? final_T[p * HW + pix] : 0.f;
     last[kk] = pv ? n_contrib[p * HW + pix] : 0;
+    max_last = max(max_last, last[kk]);
     last_alpha[kk] = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
@@ -107,18 +120,52 @@ __global__ void __launch_bounds__(256) render_backward_kernel(
       last_col[kk][c] = make_float2(0.f, 0.f);
     }
   }
+  // positions >= the CTA's largest last-contributor index are skipped by every pixel
+  __shared__ int s_maxlast;
+  if (threadIdx.x == 0) s_maxlast = 0;
+  __syncthreads();
+  atomicMax(&s_maxlast, max_last);
+  __syncthreads();
+  const int n_eff = min(n, s_maxlast);
 
-  for (int end = n; end > 0; end -= 256) {
+  for (int end = n_eff; end > 0; end -= 256) {
     const int cnt = min(256, end);
     __syncthreads();
     if ((int)threadIdx.x < cnt) {
       const int i = range.x + end - 1 - threadIdx.x;
       const int gi = point_list[i];
       s_slot[threadIdx.x] = slot_sorted[i];
-      s_r0[threadIdx.x] = rec0[gi];
-      s_cov[threadIdx.x] = cov2d[gi];
+      const float4 r0 = rec0[gi];
+      const float4 cov = cov2d[gi];
+      float wmax = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < KG; ++kk) s_w[kk][threadIdx.x] = (p0 + kk < K) ? plane_probs[gi * K + p0 + kk] : 0.f;
+      for (int kk = 0; kk < KG; ++kk) {
+        const float w = (p0 + kk < K) ? plane_probs[gi * K + p0 + kk] : 0.f;
+        s_w[kk][threadIdx.x] = w;
+        if (w >= kPlaneCutoff) wmax = fmaxf(wmax, w);
+      }
+      BwdG g;
+      g.mx = r0.x;
+      g.my = r0.y;
+      g.opacity = r0.z;
+      const float det = cov.x * cov.w - cov.y * cov.z;
+      const float det_inv = 1.0f / det;
+      g.cx = cov.w * det_inv;
+      g.cy = -cov.y * det_inv;
+      g.cz = cov.x * det_inv;
+      g.A = (cov.w * det_inv * det_inv) * cov.w;
+      g.B = (-cov.y * det_inv * det_inv) * (-cov.y);
+      g.Cc = (cov.w * det_inv * det_inv) * (-cov.y);
+      g.D = -det_inv;
+      g.E = (-cov.y * det_inv * det_inv) * cov.x;
+      g.G = (cov.x * det_inv * det_inv) * cov.x;
+      // alpha >= 1/255 needs d^T conic d <= 2 ln(255 opacity w); box of that ellipse, padded
+      const float tau = logf(255.0f * r0.z * wmax);
+      g.ok = (det != 0.0f) && (tau > 0.0f) && (wmax > 0.0f);
+      const float t2 = 2.0f * fmaxf(tau, 0.0f) * 1.01f;
+      g.ex = sqrtf(t2 * fabsf(cov.x)) * 1.01f + 0.05f;
+      g.ey = sqrtf(t2 * fabsf(cov.w)) * 1.01f + 0.05f;
+      s_g[threadIdx.x] = g;
 #pragma unroll
       for (int c = 0; c < C; ++c) {
         s_col[c][threadIdx.x] = colours[gi * C + c];
@@ -133,76 +180,68 @@ __global__ void __launch_bounds__(256) render_backward_kernel(
       for (int jl = 0; jl < nj; ++jl) {
         const int jj = jb + jl;
         const int pos = end - 1 - jj;  // 0-based position in the tile list
+        const BwdG& g = s_g[jj];
+        const float2 d = {g.mx - pxf, g.my - pyf};
+        const bool near_px = inside && g.ok && pos < max_last && fabsf(d.x) <= g.ex && fabsf(d.y) <= g.ey;
+        if (!__any_sync(0xffffffffu, near_px)) {
+          if (lane < kRedV) s_part[warp][jl][lane] = 0.f;
+          continue;
+        }
         float v[kRedV];
 #pragma unroll
         for (int i = 0; i < kRedV; ++i) v[i] = 0.f;
-        bool any = false;
-        if (inside) {
-          const float4 r0 = s_r0[jj];
-          const float4 cov = s_cov[jj];
-          const float2 d = {r0.x - pxf, r0.y - pyf};
-          const float opacity = r0.z;
-          const float det = cov.x * cov.w - cov.y * cov.z;
-#pragma unroll
-          for (int kk = 0; kk < KG; ++kk) {
-            const float plane_prob = s_w[kk][jj];
-            if (pos >= last[kk] || plane_prob < kPlaneCutoff || det == 0.0f) continue;
-            const float det_inv = 1.0f / det;
-            const float conic_x = cov.w * det_inv;
-            const float conic_y = -cov.y * det_inv;
-            const float conic_z = cov.x * det_inv;
-            const float power = -0.5f * (conic_x * d.x * d.x + conic_z * d.y * d.y) - conic_y * d.x * d.y;
-            if (power > 0.0f) continue;
+        if (near_px) {
+          const float opacity = g.opacity;
+          const float conic_x = g.cx, conic_y = g.cy, conic_z = g.cz;
+          const float power = -0.5f * (conic_x * d.x * d.x + conic_z * d.y * d.y) - conic_y * d.x * d.y;
+          if (power <= 0.0f) {
             const float G = expf(power);
-            const float alpha = min(0.99f, opacity * G * plane_prob);
-            if (alpha < 1.0f / 255.0f) continue;
-            any = true;
-            T[kk] = T[kk] / (1.0f - alpha);
-            const float dchannel_dcolor = alpha * T[kk];
-            float dL_dalpha = 0.0f;
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-              const float color = s_col[c][jj];
-              const float2 cs = s_cs[c][jj];
-              const float color_real = color * cs.x;
-              const float color_imag = color * cs.y;
-              acc_rec[kk][c].x = last_alpha[kk] * last_col[kk][c].x + (1.0f - last_alpha[kk]) * acc_rec[kk][c].x;
-              acc_rec[kk][c].y = last_alpha[kk] * last_col[kk][c].y + (1.0f - last_alpha[kk]) * acc_rec[kk][c].y;
-              last_col[kk][c] = make_float2(color_real, color_imag);
-              const float dre = dL[kk][c].x, dim = dL[kk][c].y;
-              dL_dalpha += (color_real - acc_rec[kk][c].x) * dre;
-              dL_dalpha += (color_imag - acc_rec[kk][c].y) * dim;
-              v[6 + KG + c] += dchannel_dcolor * (cs.x * dre + cs.y * dim);
-              v[6 + KG + C + c] += dchannel_dcolor * color * (-cs.y * dre + cs.x * dim);
+            for (int kk = 0; kk < KG; ++kk) {
+              const float plane_prob = s_w[kk][jj];
+              if (pos >= last[kk] || plane_prob < kPlaneCutoff) continue;
+              const float alpha = min(0.99f, opacity * G * plane_prob);
+              if (alpha < 1.0f / 255.0f) continue;
+              T[kk] = T[kk] / (1.0f - alpha);
+              const float dchannel_dcolor = alpha * T[kk];
+              float dL_dalpha = 0.0f;
+#pragma unroll
+              for (int c = 0; c < C; ++c) {
+                const float color = s_col[c][jj];
+                const float2 cs = s_cs[c][jj];
+                const float color_real = color * cs.x;
+                const float color_imag = color * cs.y;
+                acc_rec[kk][c].x = last_alpha[kk] * last_col[kk][c].x + (1.0f - last_alpha[kk]) * acc_rec[kk][c].x;
+                acc_rec[kk][c].y = last_alpha[kk] * last_col[kk][c].y + (1.0f - last_alpha[kk]) * acc_rec[kk][c].y;
+                last_col[kk][c] = make_float2(color_real, color_imag);
+                const float dre = dL[kk][c].x, dim = dL[kk][c].y;
+                dL_dalpha += (color_real - acc_rec[kk][c].x) * dre;
+                dL_dalpha += (color_imag - acc_rec[kk][c].y) * dim;
+                v[6 + KG + c] += dchannel_dcolor * (cs.x * dre + cs.y * dim);
+                v[6 + KG + C + c] += dchannel_dcolor * color * (-cs.y * dre + cs.x * dim);
+              }
+              dL_dalpha *= T[kk];
+              last_alpha[kk] = alpha;
+              const float dL_dG = opacity * plane_prob * dL_dalpha;
+              const float gdx = G * d.x;
+              const float gdy = G * d.y;
+              const float dG_ddelx = -gdx * conic_x - gdy * conic_y;
+              const float dG_ddely = -gdy * conic_z - gdx * conic_y;
+              v[0] += dL_dG * dG_ddelx * ddelx_dx;
+              v[1] += dL_dG * dG_ddely * ddely_dy;
+              const float dL_dconic_x = -0.5f * gdx * d.x * dL_dG;
+              const float dL_dconic_y = -0.5f * gdx * d.y * dL_dG;
+              const float dL_dconic_z = -0.5f * gdy * d.y * dL_dG;
+              v[2] += dL_dconic_x * g.A + dL_dconic_z * g.B;
+              v[3] += dL_dconic_x * g.Cc + dL_dconic_y * g.D + dL_dconic_z * g.E;
+              v[4] += dL_dconic_x * g.B + dL_dconic_z * g.G;
+              v[5] += G * plane_prob * dL_dalpha;
+              v[6 + kk] += opacity * G * dL_dalpha;
             }
-            dL_dalpha *= T[kk];
-            last_alpha[kk] = alpha;
-            const float dL_dG = opacity * plane_prob * dL_dalpha;
-            const float gdx = G * d.x;
-            const float gdy = G * d.y;
-            const float dG_ddelx = -gdx * conic_x - gdy * conic_y;
-            const float dG_ddely = -gdy * conic_z - gdx * conic_y;
-            v[0] += dL_dG * dG_ddelx * ddelx_dx;
-            v[1] += dL_dG * dG_ddely * ddely_dy;
-            const float dL_dconic_x = -0.5f * gdx * d.x * dL_dG;
-            const float dL_dconic_y = -0.5f * gdx * d.y * dL_dG;
-            const float dL_dconic_z = -0.5f * gdy * d.y * dL_dG;
-            v[2] += dL_dconic_x * (cov.w * det_inv * det_inv) * cov.w +
-                    dL_dconic_z * (-cov.y * det_inv * det_inv) * (-cov.y);
-            v[3] += dL_dconic_x * (cov.w * det_inv * det_inv) * (-cov.y) + dL_dconic_y * (-det_inv) +
-                    dL_dconic_z * (-cov.y * det_inv * det_inv) * cov.x;
-            v[4] += dL_dconic_x * (-cov.y * det_inv * det_inv) * (-cov.y) +
-                    dL_dconic_z * (cov.x * det_inv * det_inv) * cov.x;
-            v[5] += G * plane_prob * dL_dalpha;
-            v[6 + kk] += opacity * G * dL_dalpha;
           }
         }
-        if (__any_sync(0xffffffffu, any)) {
-          const float tot = warp_reduce_scatter16(v);
-          if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
-        } else if (lane < kRedV) {
-          s_part[warp][jl][lane] = 0.f;
-        }
+        const float tot = warp_reduce_scatter16(v);
+        if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
       }
       __syncthreads();
       const int V = 6 + KG + 2 * C;
@@ -221,6 +260,17 @@ __global__ void __launch_bounds__(256) render_backward_kernel(
         *dst = s;
       }
       __syncthreads();
+    }
+  }
+  // pairs past the CTA's last contributor get zero records
+  if (n_eff < n) {
+    const int V = VR;
+    for (int e = threadIdx.x; e < (n - n_eff) * V; e += blockDim.x) {
+      const int q = e / V, ri = e - q * V;
+      const bool mine = ri < 6 || ri >= 6 + K || (ri - 6 >= p0 && ri - 6 < p0 + KG);
+      if (!mine) continue;
+      float* dst = records + (size_t)slot_sorted[range.x + n_eff + q] * VR + ri;
+      if (!(accumulate && (ri < 6 || ri >= 6 + K))) *dst = 0.f;
     }
   }
 }

@@ -114,13 +114,21 @@ __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32
 }
 
 // renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
+//
+// Far-field skip: outside a padded box around each Gaussian, alpha < 2^-30, so the
+// reference's test_T = T * (1 - alpha) equals T exactly (1 - alpha rounds to 1) and the
+// pixel's only observable change is its last-contributor index; the dropped field
+// term is below 1e-9 of the colour.  Pixels (and whole warps) outside the box take
+// that shortcut; everything inside runs the reference arithmetic unchanged.
 template <int K, int C>
 __global__ void __launch_bounds__(256) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
-    const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs,
-    int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
-  __shared__ float4 s_r0[256];
+    const float4* __restrict__ conic, const float4* __restrict__ cov2d, const float2* __restrict__ cp,
+    const float* __restrict__ plane_probs, int W, int H, int gx, float2* __restrict__ field,
+    float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
+  __shared__ float4 s_r0[256];  // (mx, my, opacity, box half-width)
   __shared__ float4 s_cn[256];
+  __shared__ float s_ey[256];   // box half-height
   __shared__ float s_w[K][256];
   __shared__ float2 s_cp[C][256];
   const int tile = blockIdx.x;
@@ -150,10 +158,22 @@ __global__ void __launch_bounds__(256) render_forward_kernel(
     const int j = base + threadIdx.x;
     if (j < n) {
       const int gi = point_list[range.x + j];
-      s_r0[threadIdx.x] = rec0[gi];
+      float4 r0 = rec0[gi];
+      const float4 cv = cov2d[gi];
       s_cn[threadIdx.x] = conic[gi];
+      float wmax = 0.f;
 #pragma unroll
-      for (int p = 0; p < K; ++p) s_w[p][threadIdx.x] = plane_probs[gi * K + p];
+      for (int p = 0; p < K; ++p) {
+        const float w = plane_probs[gi * K + p];
+        s_w[p][threadIdx.x] = w;
+        if (w >= kPlaneCutoff) wmax = fmaxf(wmax, w);
+      }
+      // alpha >= 2^-30 needs d^T conic d <= 2 ln(opacity w 2^30): box of that ellipse, padded
+      const float t2 = 2.0f * fmaxf(logf(r0.z * wmax * 1073741824.0f), 0.0f) * 1.01f;
+      r0.w = sqrtf(t2 * fabsf(cv.x)) * 1.01f + 0.05f;
+      s_ey[threadIdx.x] = sqrtf(t2 * fabsf(cv.w)) * 1.01f + 0.05f;
+      if (!(r0.w == r0.w) || !(s_ey[threadIdx.x] == s_ey[threadIdx.x])) { r0.w = 3.4e38f; s_ey[threadIdx.x] = 3.4e38f; }
+      s_r0[threadIdx.x] = r0;
 #pragma unroll
       for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
     }
@@ -162,6 +182,13 @@ __global__ void __launch_bounds__(256) render_forward_kernel(
     for (int jj = 0; jj < cnt && !alldone; ++jj) {
       const float4 r0 = s_r0[jj];
       const float2 d = {r0.x - pxf, r0.y - pyf};
+      if (fabsf(d.x) > r0.w || fabsf(d.y) > s_ey[jj]) {
+        // far field: power << 0 and 1 - alpha == 1, so only the last-contributor index moves
+#pragma unroll
+        for (int p = 0; p < K; ++p)
+          if (!done[p] && s_w[p][jj] >= kPlaneCutoff) last[p] = base + jj + 1;
+        continue;
+      }
       const float4 cn = s_cn[jj];
       const float inv00 = cn.x, inv01 = cn.y, inv10 = cn.z, inv11 = cn.w;
       const float power = -0.5f * (d.x * (inv00 * d.x + inv10 * d.y) + d.y * (inv01 * d.x + inv11 * d.y));
@@ -207,9 +234,9 @@ template <int K>
 int launch_render_k(int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
                     const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
   switch (C) {
-    case 1: render_forward_kernel<K, 1><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
-    case 2: render_forward_kernel<K, 2><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
-    default: render_forward_kernel<K, 3><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 1: render_forward_kernel<K, 1><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 2: render_forward_kernel<K, 2><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
+    default: render_forward_kernel<K, 3><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
