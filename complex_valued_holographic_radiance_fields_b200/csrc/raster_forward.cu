@@ -115,118 +115,121 @@ __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32
 
 // renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
 //
-// Far-field skip: outside a padded box around each Gaussian, alpha < 2^-30, so the
-// reference's test_T = T * (1 - alpha) equals T exactly (1 - alpha rounds to 1) and the
-// pixel's only observable change is its last-contributor index; the dropped field
-// term is below 1e-9 of the colour.  Pixels (and whole warps) outside the box take
-// that shortcut; everything inside runs the reference arithmetic unchanged.
+// 128 threads per 16x16 tile; each thread owns two horizontally adjacent pixels and
+// evaluates both with packed f32x2 arithmetic (sm_100 FFMA2/FMUL2/FADD2).  Every lane
+// of a packed operation is an ordinary IEEE-rounded float operation, so each pixel
+// sees the reference's arithmetic: power = -0.5 (dx (i00 dx + i10 dy) + dy (i01 dx +
+// i11 dy)), G = expf(power), alpha = min(0.99, (o G) w), T' = T (1 - alpha), done when
+// T' < 1e-4, last = 1-based position of the last contributor.  A pixel that is done or
+// outside the image contributes through a zero weight (acc + 0 * c == acc).
 template <int K, int C>
-__global__ void __launch_bounds__(256) render_forward_kernel(
+__global__ void __launch_bounds__(128) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
-    const float4* __restrict__ conic, const float4* __restrict__ cov2d, const float2* __restrict__ cp,
-    const float* __restrict__ plane_probs, int W, int H, int gx, float2* __restrict__ field,
-    float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
-  __shared__ float4 s_r0[256];  // (mx, my, opacity, box half-width)
-  __shared__ float4 s_cn[256];
-  __shared__ float s_ey[256];   // box half-height
-  __shared__ float s_w[K][256];
-  __shared__ float2 s_cp[C][256];
+    const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs,
+    int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
+  constexpr int NB = 128;  // Gaussians staged per batch
+  __shared__ float2 s_m[NB];       // mean
+  __shared__ float2 s_o[NB];       // (opacity, -)
+  __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
+  __shared__ float4 s_c1[NB];      // (i10, i10, i11, i11)
+  __shared__ float s_w[K][NB];
+  __shared__ float2 s_cp[C][NB];
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
-  const int px = tx * kTile + (threadIdx.x & 15), py = ty * kTile + (threadIdx.x >> 4);
-  const bool inside = px < W && py < H;
-  const float pxf = (float)px, pyf = (float)py;
+  const int lx = (threadIdx.x & 7) * 2, ly = threadIdx.x >> 3;
+  const int px = tx * kTile + lx, py = ty * kTile + ly;
+  const bool in0 = px < W && py < H, in1 = px + 1 < W && py < H;
+  const float2 npx = make_float2(-(float)px, -(float)(px + 1));
+  const float pyf = (float)py;
   const int2 range = ranges[tile];
   const int n = range.y - range.x;
 
-  float T[K];
-  int last[K];
-  bool done[K];
-  float2 acc[K][C];
+  float2 T[K];
+  int last0[K], last1[K];
+  bool done0[K], done1[K];
+  float2 acc0[K][C], acc1[K][C];
 #pragma unroll
   for (int p = 0; p < K; ++p) {
-    T[p] = 1.0f;
-    last[p] = 0;
-    done[p] = !inside;
+    T[p] = make_float2(1.0f, 1.0f);
+    last0[p] = last1[p] = 0;
+    done0[p] = !in0;
+    done1[p] = !in1;
 #pragma unroll
-    for (int c = 0; c < C; ++c) acc[p][c] = make_float2(0.f, 0.f);
+    for (int c = 0; c < C; ++c) acc0[p][c] = acc1[p][c] = make_float2(0.f, 0.f);
   }
-  bool alldone = !inside;
+  bool alldone = !in0 && !in1;
 
-  for (int base = 0; base < n; base += 256) {
+  for (int base = 0; base < n; base += NB) {
     if (__syncthreads_and(alldone)) break;
-    const int j = base + threadIdx.x;
-    if (j < n) {
-      const int gi = point_list[range.x + j];
-      float4 r0 = rec0[gi];
-      const float4 cv = cov2d[gi];
-      s_cn[threadIdx.x] = conic[gi];
-      float wmax = 0.f;
+    {
+      const int j = base + threadIdx.x;
+      if (j < n) {
+        const int gi = point_list[range.x + j];
+        const float4 r0 = rec0[gi];
+        const float4 cn = conic[gi];
+        s_m[threadIdx.x] = make_float2(r0.x, r0.y);
+        s_o[threadIdx.x] = make_float2(r0.z, r0.z);
+        s_c0[threadIdx.x] = make_float4(cn.x, cn.x, cn.y, cn.y);
+        s_c1[threadIdx.x] = make_float4(cn.z, cn.z, cn.w, cn.w);
 #pragma unroll
-      for (int p = 0; p < K; ++p) {
-        const float w = plane_probs[gi * K + p];
-        s_w[p][threadIdx.x] = w;
-        if (w >= kPlaneCutoff) wmax = fmaxf(wmax, w);
+        for (int p = 0; p < K; ++p) s_w[p][threadIdx.x] = plane_probs[gi * K + p];
+#pragma unroll
+        for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
       }
-      // alpha >= 2^-30 needs d^T conic d <= 2 ln(opacity w 2^30): box of that ellipse, padded
-      const float t2 = 2.0f * fmaxf(logf(r0.z * wmax * 1073741824.0f), 0.0f) * 1.01f;
-      r0.w = sqrtf(t2 * fabsf(cv.x)) * 1.01f + 0.05f;
-      s_ey[threadIdx.x] = sqrtf(t2 * fabsf(cv.w)) * 1.01f + 0.05f;
-      if (!(r0.w == r0.w) || !(s_ey[threadIdx.x] == s_ey[threadIdx.x])) { r0.w = 3.4e38f; s_ey[threadIdx.x] = 3.4e38f; }
-      s_r0[threadIdx.x] = r0;
-#pragma unroll
-      for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
     }
     __syncthreads();
-    const int cnt = min(256, n - base);
+    const int cnt = min(NB, n - base);
     for (int jj = 0; jj < cnt && !alldone; ++jj) {
-      const float4 r0 = s_r0[jj];
-      const float2 d = {r0.x - pxf, r0.y - pyf};
-      if (fabsf(d.x) > r0.w || fabsf(d.y) > s_ey[jj]) {
-        // far field: power << 0 and 1 - alpha == 1, so only the last-contributor index moves
-#pragma unroll
-        for (int p = 0; p < K; ++p)
-          if (!done[p] && s_w[p][jj] >= kPlaneCutoff) last[p] = base + jj + 1;
-        continue;
-      }
-      const float4 cn = s_cn[jj];
-      const float inv00 = cn.x, inv01 = cn.y, inv10 = cn.z, inv11 = cn.w;
-      const float power = -0.5f * (d.x * (inv00 * d.x + inv10 * d.y) + d.y * (inv01 * d.x + inv11 * d.y));
-      if (power > 0.0f) continue;
-      const float og = r0.z * expf(power);
+      const float2 m = s_m[jj];
+      const float2 dx = __fadd2_rn(make_float2(m.x, m.x), npx);
+      const float dys = m.y - pyf;
+      const float2 dy = make_float2(dys, dys);
+      const float4 c0 = s_c0[jj], c1 = s_c1[jj];
+      const float2 u = __ffma2_rn(make_float2(c0.x, c0.y), dx, __fmul2_rn(make_float2(c1.x, c1.y), dy));
+      const float2 v = __ffma2_rn(make_float2(c0.z, c0.w), dx, __fmul2_rn(make_float2(c1.z, c1.w), dy));
+      const float2 power = __fmul2_rn(make_float2(-0.5f, -0.5f), __ffma2_rn(dx, u, __fmul2_rn(dy, v)));
+      const bool ok0 = power.x <= 0.0f, ok1 = power.y <= 0.0f;
+      if (!ok0 && !ok1) continue;
+      const float2 og = __fmul2_rn(s_o[jj], make_float2(expf(power.x), expf(power.y)));
+      const int pos = base + jj + 1;
       bool all = true;
 #pragma unroll
       for (int p = 0; p < K; ++p) {
-        if (!done[p]) {
-          const float w = s_w[p][jj];
-          if (w >= kPlaneCutoff) {
-            const float alpha = fminf(kMaxAlpha, og * w);
-            const float test_T = T[p] * (1.0f - alpha);
-            if (test_T < 0.0001f) done[p] = true;
-            const float wt = alpha * T[p];
+        const float w = s_w[p][jj];
+        if (w >= kPlaneCutoff) {
+          const bool a0 = ok0 && !done0[p], a1 = ok1 && !done1[p];
+          if (a0 || a1) {
+            const float2 aw = __fmul2_rn(og, make_float2(w, w));
+            const float2 alpha = make_float2(fminf(kMaxAlpha, aw.x), fminf(kMaxAlpha, aw.y));
+            const float2 test = __fmul2_rn(T[p], __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(-alpha.x, -alpha.y)));
+            const float2 wt = __fmul2_rn(alpha, T[p]);
+            const float2 wt0 = make_float2(a0 ? wt.x : 0.f, a0 ? wt.x : 0.f);
+            const float2 wt1 = make_float2(a1 ? wt.y : 0.f, a1 ? wt.y : 0.f);
 #pragma unroll
             for (int c = 0; c < C; ++c) {
-              const float2 v = s_cp[c][jj];
-              acc[p][c].x = fmaf(wt, v.x, acc[p][c].x);
-              acc[p][c].y = fmaf(wt, v.y, acc[p][c].y);
+              const float2 col = s_cp[c][jj];
+              acc0[p][c] = __ffma2_rn(wt0, col, acc0[p][c]);
+              acc1[p][c] = __ffma2_rn(wt1, col, acc1[p][c]);
             }
-            T[p] = test_T;
-            last[p] = base + jj + 1;
+            if (a0) { T[p].x = test.x; last0[p] = pos; done0[p] = test.x < 0.0001f; }
+            if (a1) { T[p].y = test.y; last1[p] = pos; done1[p] = test.y < 0.0001f; }
           }
         }
-        all = all && done[p];
+        all = all && done0[p] && done1[p];
       }
       alldone = all;
     }
   }
-  if (!inside) return;
   const size_t HW = (size_t)H * W, pix = (size_t)py * W + px;
 #pragma unroll
   for (int p = 0; p < K; ++p) {
 #pragma unroll
-    for (int c = 0; c < C; ++c) field[(p * C + c) * HW + pix] = acc[p][c];
-    final_T[p * HW + pix] = T[p];
-    n_contrib[p * HW + pix] = last[p];
+    for (int c = 0; c < C; ++c) {
+      if (in0) field[(p * C + c) * HW + pix] = acc0[p][c];
+      if (in1) field[(p * C + c) * HW + pix + 1] = acc1[p][c];
+    }
+    if (in0) { final_T[p * HW + pix] = T[p].x; n_contrib[p * HW + pix] = last0[p]; }
+    if (in1) { final_T[p * HW + pix + 1] = T[p].y; n_contrib[p * HW + pix + 1] = last1[p]; }
   }
 }
 
@@ -234,9 +237,9 @@ template <int K>
 int launch_render_k(int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
                     const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
   switch (C) {
-    case 1: render_forward_kernel<K, 1><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
-    case 2: render_forward_kernel<K, 2><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
-    default: render_forward_kernel<K, 3><<<grid, 256, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cov2d, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 1: render_forward_kernel<K, 1><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 2: render_forward_kernel<K, 2><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    default: render_forward_kernel<K, 3><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
