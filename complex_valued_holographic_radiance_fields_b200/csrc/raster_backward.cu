@@ -61,216 +61,236 @@ __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[kRedV]) {
 }
 
 // Per-Gaussian constants of the backward pixel loop, computed once per batch with the
-// reference's expressions (backward_splat.cu:194-206, 283-292), so the per-pixel
-// arithmetic is unchanged; plus a conservative bounding box of the region where
-// alpha >= 1/255 can hold (outside it the reference `continue`s, :218).
+// reference's expressions (backward_splat.cu:194-206, 283-292), plus a conservative
+// bounding box of the region where alpha >= 1/255 can hold (outside it the reference
+// `continue`s, :218).
 struct BwdG {
   float mx, my, opacity, ex;      // mean, opacity, box half-width
   float cx, cy, cz, ey;           // conic_x, conic_y, conic_z, box half-height
   float A, B, Cc, D;              // d cov / d conic coefficients
-  float E, G;                     // (A..G: see render_backward_kernel)
-  int ok;                         // det != 0 and the box is non-empty
+  float E, G;
 };
 
-template <int KG, int C>
-__global__ void __launch_bounds__(256) render_backward_kernel(
+// Per-pixel state of one plane's back-to-front replay (backward_splat.cu:133-148).
+template <int C>
+struct PixState {
+  float T, la;                    // transmittance, last alpha
+  int last;                       // n_contrib: positions >= last are skipped
+  float2 dL[C], acc[C], lc[C];    // dL/dpixel, accumulated colour, last colour
+};
+
+// One pixel, one Gaussian: renderBackwardTileKernel's arithmetic (:184-300), adding this
+// pixel's gradient contributions into v (6 + 1 + 2C entries).
+template <int C>
+__device__ __forceinline__ void bwd_pixel(PixState<C>& st, const BwdG& g, float w, float2 d,
+                                          const float2* cpx, const float2* cs, float ddelx_dx, float ddely_dy,
+                                          float* v) {
+  const float power = -0.5f * (g.cx * d.x * d.x + g.cz * d.y * d.y) - g.cy * d.x * d.y;
+  if (power > 0.0f) return;
+  const float G = expf(power);
+  const float alpha = min(0.99f, g.opacity * G * w);
+  if (alpha < 1.0f / 255.0f) return;
+  st.T = st.T / (1.0f - alpha);
+  const float dch = alpha * st.T;
+  const float2 la2 = make_float2(st.la, st.la);
+  const float2 nla2 = make_float2(1.0f - st.la, 1.0f - st.la);
+  float dL_dalpha = 0.0f;
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    st.acc[c] = __ffma2_rn(la2, st.lc[c], __fmul2_rn(nla2, st.acc[c]));
+    st.lc[c] = cpx[c];
+    const float2 t = __fmul2_rn(__fadd2_rn(cpx[c], make_float2(-st.acc[c].x, -st.acc[c].y)), st.dL[c]);
+    dL_dalpha += t.x;
+    dL_dalpha += t.y;
+    v[7 + c] += dch * (cs[c].x * st.dL[c].x + cs[c].y * st.dL[c].y);
+    v[7 + C + c] += dch * (-cpx[c].y * st.dL[c].x + cpx[c].x * st.dL[c].y);
+  }
+  dL_dalpha *= st.T;
+  st.la = alpha;
+  const float dL_dG = g.opacity * w * dL_dalpha;
+  const float gdx = G * d.x, gdy = G * d.y;
+  v[0] += dL_dG * (-gdx * g.cx - gdy * g.cy) * ddelx_dx;
+  v[1] += dL_dG * (-gdy * g.cz - gdx * g.cy) * ddely_dy;
+  const float dcx = -0.5f * gdx * d.x * dL_dG;
+  const float dcy = -0.5f * gdx * d.y * dL_dG;
+  const float dcz = -0.5f * gdy * d.y * dL_dG;
+  v[2] += dcx * g.A + dcz * g.B;
+  v[3] += dcx * g.Cc + dcy * g.D + dcz * g.E;
+  v[4] += dcx * g.B + dcz * g.G;
+  v[5] += G * w * dL_dalpha;
+  v[6] += g.opacity * G * dL_dalpha;
+}
+
+// One CTA per 16x16 tile, 128 threads x 2 horizontally adjacent pixels, one pass per
+// plane.  Each pass stages the tile list back to front in batches, keeps only the
+// Gaussians that can contribute on this plane inside this tile (plane weight >= 1e-6,
+// alpha >= 1/255 box meets the tile, position below the tile's largest n_contrib), and
+// for each of those reduces the per-pixel contributions over the CTA into the pair's
+// record (records start at zero; each pass adds its plane's share).
+template <int C>
+__global__ void __launch_bounds__(128, 3) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
     const float4* __restrict__ rec0, const float4* __restrict__ cov2d, const float* __restrict__ colours,
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
-    int p0, int accumulate, float* __restrict__ records) {
-  constexpr int NW = 8;
-  static_assert(6 + KG + 2 * C <= kRedV, "reduction vector too long");
-  __shared__ uint32_t s_slot[256];
-  __shared__ BwdG s_g[256];
-  __shared__ float s_w[KG][256];
-  __shared__ float s_col[C][256];
-  __shared__ float2 s_cs[C][256];
+    float* __restrict__ records) {
+  constexpr int NB = 128, NW = 4;
+  static_assert(7 + 2 * C <= kRedV, "reduction vector too long");
+  __shared__ uint32_t s_slot[NB];
+  __shared__ int s_pos[NB];
+  __shared__ BwdG s_g[NB];
+  __shared__ float s_w[NB];
+  __shared__ float2 s_cpx[C][NB];
+  __shared__ float2 s_cs[C][NB];
   __shared__ float s_part[NW][32][kRedV];
+  __shared__ int s_wcnt[NW];
+  __shared__ int s_maxlast;
 
   const int VR = 6 + K + 2 * C;
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int px = tx * kTile + (threadIdx.x & 15), py = ty * kTile + (threadIdx.x >> 4);
-  const bool inside = px < W && py < H;
-  const float pxf = (float)px, pyf = (float)py;
+  const int px = tx * kTile + (threadIdx.x & 7) * 2, py = ty * kTile + (threadIdx.x >> 3);
+  const bool in0 = px < W && py < H, in1 = px + 1 < W && py < H;
+  const float2 p0f = make_float2((float)px, (float)py), p1f = make_float2((float)(px + 1), (float)py);
   const int2 range = ranges[tile];
   const int n = range.y - range.x;
   if (n <= 0) return;
-  const size_t HW = (size_t)H * W, pix = inside ? (size_t)py * W + px : 0;
+  const size_t HW = (size_t)H * W;
+  const size_t pix0 = in0 ? (size_t)py * W + px : 0, pix1 = in1 ? (size_t)py * W + px + 1 : 0;
   const float ddelx_dx = 0.5f * W, ddely_dy = 0.5f * H;
+  const float tx0 = (float)(tx * kTile), tx1 = (float)(tx * kTile + kTile - 1);
+  const float ty0 = (float)(ty * kTile), ty1 = (float)(ty * kTile + kTile - 1);
+  const unsigned lt = (1u << lane) - 1u;
 
-  float T[KG], last_alpha[KG];
-  int last[KG];
-  float2 dL[KG][C], acc_rec[KG][C], last_col[KG][C];
-  int max_last = 0;
-#pragma unroll
-  for (int kk = 0; kk < KG; ++kk) {
-    const int p = p0 + kk;
-    const bool pv = inside && p < K;
-    T[kk] = pv ? final_T[p * HW + pix] : 0.f;
-    last[kk] = pv ? n_contrib[p * HW + pix] : 0;
-    max_last = max(max_last, last[kk]);
-    last_alpha[kk] = 0.f;
+  for (int p = 0; p < K; ++p) {
+    PixState<C> s0, s1;
+    s0.T = in0 ? final_T[p * HW + pix0] : 0.f;
+    s1.T = in1 ? final_T[p * HW + pix1] : 0.f;
+    s0.last = in0 ? n_contrib[p * HW + pix0] : 0;
+    s1.last = in1 ? n_contrib[p * HW + pix1] : 0;
+    s0.la = s1.la = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      dL[kk][c] = pv ? grad_field[(size_t)(p * C + c) * HW + pix] : make_float2(0.f, 0.f);
-      acc_rec[kk][c] = make_float2(0.f, 0.f);
-      last_col[kk][c] = make_float2(0.f, 0.f);
+      s0.dL[c] = in0 ? grad_field[(size_t)(p * C + c) * HW + pix0] : make_float2(0.f, 0.f);
+      s1.dL[c] = in1 ? grad_field[(size_t)(p * C + c) * HW + pix1] : make_float2(0.f, 0.f);
+      s0.acc[c] = s1.acc[c] = s0.lc[c] = s1.lc[c] = make_float2(0.f, 0.f);
     }
-  }
-  // positions >= the CTA's largest last-contributor index are skipped by every pixel
-  __shared__ int s_maxlast;
-  if (threadIdx.x == 0) s_maxlast = 0;
-  __syncthreads();
-  atomicMax(&s_maxlast, max_last);
-  __syncthreads();
-  const int n_eff = min(n, s_maxlast);
+    __syncthreads();
+    if (threadIdx.x == 0) s_maxlast = 0;
+    __syncthreads();
+    atomicMax(&s_maxlast, max(s0.last, s1.last));
+    __syncthreads();
+    const int n_eff = min(n, s_maxlast);
 
-  for (int end = n_eff; end > 0; end -= 256) {
-    const int cnt = min(256, end);
-    __syncthreads();
-    if ((int)threadIdx.x < cnt) {
-      const int i = range.x + end - 1 - threadIdx.x;
-      const int gi = point_list[i];
-      s_slot[threadIdx.x] = slot_sorted[i];
-      const float4 r0 = rec0[gi];
-      const float4 cov = cov2d[gi];
-      float wmax = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < KG; ++kk) {
-        const float w = (p0 + kk < K) ? plane_probs[gi * K + p0 + kk] : 0.f;
-        s_w[kk][threadIdx.x] = w;
-        if (w >= kPlaneCutoff) wmax = fmaxf(wmax, w);
-      }
+    for (int end = n_eff; end > 0; end -= NB) {
+      const int cnt = min(NB, end);
+      // ---- stage and compact this batch (order kept: back to front) ----
+      bool keep = false;
       BwdG g;
-      g.mx = r0.x;
-      g.my = r0.y;
-      g.opacity = r0.z;
-      const float det = cov.x * cov.w - cov.y * cov.z;
-      const float det_inv = 1.0f / det;
-      g.cx = cov.w * det_inv;
-      g.cy = -cov.y * det_inv;
-      g.cz = cov.x * det_inv;
-      g.A = (cov.w * det_inv * det_inv) * cov.w;
-      g.B = (-cov.y * det_inv * det_inv) * (-cov.y);
-      g.Cc = (cov.w * det_inv * det_inv) * (-cov.y);
-      g.D = -det_inv;
-      g.E = (-cov.y * det_inv * det_inv) * cov.x;
-      g.G = (cov.x * det_inv * det_inv) * cov.x;
-      // alpha >= 1/255 needs d^T conic d <= 2 ln(255 opacity w); box of that ellipse, padded
-      const float tau = logf(255.0f * r0.z * wmax);
-      g.ok = (det != 0.0f) && (tau > 0.0f) && (wmax > 0.0f);
-      const float t2 = 2.0f * fmaxf(tau, 0.0f) * 1.01f;
-      g.ex = sqrtf(t2 * fabsf(cov.x)) * 1.01f + 0.05f;
-      g.ey = sqrtf(t2 * fabsf(cov.w)) * 1.01f + 0.05f;
-      s_g[threadIdx.x] = g;
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        s_col[c][threadIdx.x] = colours[gi * C + c];
-        float sn, cs;
-        __sincosf(phase[gi * C + c], &sn, &cs);
-        s_cs[c][threadIdx.x] = make_float2(cs, sn);
-      }
-    }
-    __syncthreads();
-    for (int jb = 0; jb < cnt; jb += 32) {
-      const int nj = min(32, cnt - jb);
-      for (int jl = 0; jl < nj; ++jl) {
-        const int jj = jb + jl;
-        const int pos = end - 1 - jj;  // 0-based position in the tile list
-        const BwdG& g = s_g[jj];
-        const float2 d = {g.mx - pxf, g.my - pyf};
-        const bool near_px = inside && g.ok && pos < max_last && fabsf(d.x) <= g.ex && fabsf(d.y) <= g.ey;
-        if (!__any_sync(0xffffffffu, near_px)) {
-          if (lane < kRedV) s_part[warp][jl][lane] = 0.f;
-          continue;
+      float w = 0.f;
+      int gi = 0, pos = 0;
+      if ((int)threadIdx.x < cnt) {
+        pos = end - 1 - threadIdx.x;
+        gi = point_list[range.x + pos];
+        w = plane_probs[gi * K + p];
+        if (w >= kPlaneCutoff) {
+          const float4 r0 = rec0[gi];
+          const float4 cov = cov2d[gi];
+          g.mx = r0.x;
+          g.my = r0.y;
+          g.opacity = r0.z;
+          const float det = cov.x * cov.w - cov.y * cov.z;
+          const float det_inv = 1.0f / det;
+          g.cx = cov.w * det_inv;
+          g.cy = -cov.y * det_inv;
+          g.cz = cov.x * det_inv;
+          g.A = (cov.w * det_inv * det_inv) * cov.w;
+          g.B = (-cov.y * det_inv * det_inv) * (-cov.y);
+          g.Cc = (cov.w * det_inv * det_inv) * (-cov.y);
+          g.D = -det_inv;
+          g.E = (-cov.y * det_inv * det_inv) * cov.x;
+          g.G = (cov.x * det_inv * det_inv) * cov.x;
+          // alpha >= 1/255 needs d^T conic d <= 2 ln(255 opacity w): padded box of that ellipse
+          const float tau = logf(255.0f * r0.z * w);
+          const float t2 = 2.0f * fmaxf(tau, 0.0f) * 1.01f;
+          g.ex = sqrtf(t2 * fabsf(cov.x)) * 1.01f + 0.05f;
+          g.ey = sqrtf(t2 * fabsf(cov.w)) * 1.01f + 0.05f;
+          keep = det != 0.0f && tau > 0.0f && g.mx + g.ex >= tx0 && g.mx - g.ex <= tx1 && g.my + g.ey >= ty0 &&
+                 g.my - g.ey <= ty1;
         }
-        float v[kRedV];
+      }
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      __syncthreads();  // previous batch fully consumed
+      if (lane == 0) s_wcnt[warp] = __popc(bal);
+      __syncthreads();
+      int off = 0, total = 0;
 #pragma unroll
-        for (int i = 0; i < kRedV; ++i) v[i] = 0.f;
-        if (near_px) {
-          const float opacity = g.opacity;
-          const float conic_x = g.cx, conic_y = g.cy, conic_z = g.cz;
-          const float power = -0.5f * (conic_x * d.x * d.x + conic_z * d.y * d.y) - conic_y * d.x * d.y;
-          if (power <= 0.0f) {
-            const float G = expf(power);
+      for (int w2 = 0; w2 < NW; ++w2) {
+        off += w2 < warp ? s_wcnt[w2] : 0;
+        total += s_wcnt[w2];
+      }
+      if (keep) {
+        const int idx = off + __popc(bal & lt);
+        s_slot[idx] = slot_sorted[range.x + pos];
+        s_pos[idx] = pos;
+        s_g[idx] = g;
+        s_w[idx] = w;
 #pragma unroll
-            for (int kk = 0; kk < KG; ++kk) {
-              const float plane_prob = s_w[kk][jj];
-              if (pos >= last[kk] || plane_prob < kPlaneCutoff) continue;
-              const float alpha = min(0.99f, opacity * G * plane_prob);
-              if (alpha < 1.0f / 255.0f) continue;
-              T[kk] = T[kk] / (1.0f - alpha);
-              const float dchannel_dcolor = alpha * T[kk];
-              float dL_dalpha = 0.0f;
-#pragma unroll
-              for (int c = 0; c < C; ++c) {
-                const float color = s_col[c][jj];
-                const float2 cs = s_cs[c][jj];
-                const float color_real = color * cs.x;
-                const float color_imag = color * cs.y;
-                acc_rec[kk][c].x = last_alpha[kk] * last_col[kk][c].x + (1.0f - last_alpha[kk]) * acc_rec[kk][c].x;
-                acc_rec[kk][c].y = last_alpha[kk] * last_col[kk][c].y + (1.0f - last_alpha[kk]) * acc_rec[kk][c].y;
-                last_col[kk][c] = make_float2(color_real, color_imag);
-                const float dre = dL[kk][c].x, dim = dL[kk][c].y;
-                dL_dalpha += (color_real - acc_rec[kk][c].x) * dre;
-                dL_dalpha += (color_imag - acc_rec[kk][c].y) * dim;
-                v[6 + KG + c] += dchannel_dcolor * (cs.x * dre + cs.y * dim);
-                v[6 + KG + C + c] += dchannel_dcolor * color * (-cs.y * dre + cs.x * dim);
-              }
-              dL_dalpha *= T[kk];
-              last_alpha[kk] = alpha;
-              const float dL_dG = opacity * plane_prob * dL_dalpha;
-              const float gdx = G * d.x;
-              const float gdy = G * d.y;
-              const float dG_ddelx = -gdx * conic_x - gdy * conic_y;
-              const float dG_ddely = -gdy * conic_z - gdx * conic_y;
-              v[0] += dL_dG * dG_ddelx * ddelx_dx;
-              v[1] += dL_dG * dG_ddely * ddely_dy;
-              const float dL_dconic_x = -0.5f * gdx * d.x * dL_dG;
-              const float dL_dconic_y = -0.5f * gdx * d.y * dL_dG;
-              const float dL_dconic_z = -0.5f * gdy * d.y * dL_dG;
-              v[2] += dL_dconic_x * g.A + dL_dconic_z * g.B;
-              v[3] += dL_dconic_x * g.Cc + dL_dconic_y * g.D + dL_dconic_z * g.E;
-              v[4] += dL_dconic_x * g.B + dL_dconic_z * g.G;
-              v[5] += G * plane_prob * dL_dalpha;
-              v[6 + kk] += opacity * G * dL_dalpha;
-            }
+        for (int c = 0; c < C; ++c) {
+          float sn, cs;
+          __sincosf(phase[gi * C + c], &sn, &cs);
+          const float col = colours[gi * C + c];
+          s_cs[c][idx] = make_float2(cs, sn);
+          s_cpx[c][idx] = make_float2(col * cs, col * sn);
+        }
+      }
+      __syncthreads();
+      // ---- replay the kept Gaussians, 32 at a time ----
+      for (int jb = 0; jb < total; jb += 32) {
+        const int nj = min(32, total - jb);
+        for (int jl = 0; jl < nj; ++jl) {
+          const int jj = jb + jl;
+          const BwdG& gg = s_g[jj];
+          const int q = s_pos[jj];
+          const float2 d0 = make_float2(gg.mx - p0f.x, gg.my - p0f.y);
+          const float2 d1 = make_float2(gg.mx - p1f.x, gg.my - p1f.y);
+          const bool ny = fabsf(d0.y) <= gg.ey;
+          const bool n0 = in0 && q < s0.last && ny && fabsf(d0.x) <= gg.ex;
+          const bool n1 = in1 && q < s1.last && ny && fabsf(d1.x) <= gg.ex;
+          if (!__any_sync(0xffffffffu, n0 || n1)) {
+            if (lane < kRedV) s_part[warp][jl][lane] = 0.f;
+            continue;
           }
-        }
-        const float tot = warp_reduce_scatter16(v);
-        if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
-      }
-      __syncthreads();
-      const int V = 6 + KG + 2 * C;
-      for (int e = threadIdx.x; e < nj * kRedV; e += blockDim.x) {
-        const int jl = e / kRedV, idx = e - jl * kRedV;
-        if (idx >= V) continue;
-        float s = 0.f;
+          float v[kRedV];
 #pragma unroll
-        for (int w = 0; w < NW; ++w) s += s_part[w][jl][idx];
-        int ri;
-        if (idx < 6) ri = idx;
-        else if (idx < 6 + KG) { const int p = p0 + idx - 6; if (p >= K) continue; ri = 6 + p; }
-        else ri = 6 + K + (idx - 6 - KG);
-        float* dst = records + (size_t)s_slot[jb + jl] * VR + ri;
-        if (accumulate && (idx < 6 || idx >= 6 + KG)) s += *dst;
-        *dst = s;
+          for (int i = 0; i < kRedV; ++i) v[i] = 0.f;
+          float2 cpx[C], cs[C];
+#pragma unroll
+          for (int c = 0; c < C; ++c) {
+            cpx[c] = s_cpx[c][jj];
+            cs[c] = s_cs[c][jj];
+          }
+          const float ww = s_w[jj];
+          if (n0) bwd_pixel<C>(s0, gg, ww, d0, cpx, cs, ddelx_dx, ddely_dy, v);
+          if (n1) bwd_pixel<C>(s1, gg, ww, d1, cpx, cs, ddelx_dx, ddely_dy, v);
+          const float tot = warp_reduce_scatter16(v);
+          if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
+        }
+        __syncthreads();
+        const int V = 7 + 2 * C;
+        for (int e = threadIdx.x; e < nj * kRedV; e += blockDim.x) {
+          const int jl = e / kRedV, idx = e - jl * kRedV;
+          if (idx >= V) continue;
+          float sum = 0.f;
+#pragma unroll
+          for (int w2 = 0; w2 < NW; ++w2) sum += s_part[w2][jl][idx];
+          const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
+          float* dst = records + (size_t)s_slot[jb + jl] * VR + ri;
+          *dst += sum;
+        }
+        __syncthreads();
       }
-      __syncthreads();
-    }
-  }
-  // pairs past the CTA's last contributor get zero records
-  if (n_eff < n) {
-    const int V = VR;
-    for (int e = threadIdx.x; e < (n - n_eff) * V; e += blockDim.x) {
-      const int q = e / V, ri = e - q * V;
-      const bool mine = ri < 6 || ri >= 6 + K || (ri - 6 >= p0 && ri - 6 < p0 + KG);
-      if (!mine) continue;
-      float* dst = records + (size_t)slot_sorted[range.x + n_eff + q] * VR + ri;
-      if (!(accumulate && (ri < 6 || ri >= 6 + K))) *dst = 0.f;
     }
   }
 }
@@ -310,22 +330,6 @@ __global__ void __launch_bounds__(128) gaussian_grad_kernel(cvhrf_raster_scene s
   }
 }
 
-template <int KG>
-void launch_bwd_kg(int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const uint32_t* slot,
-                   const GeomWs& g, const cvhrf_raster_scene& s, const float* fT, const int32_t* nc,
-                   const float2* gf, int gx, int p0, int accumulate, float* rec) {
-#define CVHRF_BWD(CC)                                                                                          \
-  render_backward_kernel<KG, CC><<<grid, 256, 0, st>>>(ranges, pl, slot, g.rec0, g.cov2d, s.colours, s.phase,   \
-                                                       s.plane_probs, fT, nc, gf, s.K, s.W, s.H, gx, p0,        \
-                                                       accumulate, rec)
-  switch (C) {
-    case 1: CVHRF_BWD(1); break;
-    case 2: CVHRF_BWD(2); break;
-    default: CVHRF_BWD(3); break;
-  }
-#undef CVHRF_BWD
-}
-
 }  // namespace
 }  // namespace cvhrf
 
@@ -362,17 +366,20 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
     const int T = cam.grid_x * cam.grid_y;
     dim3 grid(T);
     const int32_t* pl = point_list;
-    const int KG = s.K <= 4 ? s.K : 4;
-    for (int p0 = 0; p0 < s.K; p0 += KG) {
-      const int acc = p0 > 0 ? 1 : 0;
-      switch (KG) {
-        case 1: launch_bwd_kg<1>(s.C, grid, st, (const int2*)ranges, pl, b.slot, g, s, final_Ts, n_contrib, (const float2*)grad_field, cam.grid_x, p0, acc, rec); break;
-        case 2: launch_bwd_kg<2>(s.C, grid, st, (const int2*)ranges, pl, b.slot, g, s, final_Ts, n_contrib, (const float2*)grad_field, cam.grid_x, p0, acc, rec); break;
-        case 3: launch_bwd_kg<3>(s.C, grid, st, (const int2*)ranges, pl, b.slot, g, s, final_Ts, n_contrib, (const float2*)grad_field, cam.grid_x, p0, acc, rec); break;
-        default: launch_bwd_kg<4>(s.C, grid, st, (const int2*)ranges, pl, b.slot, g, s, final_Ts, n_contrib, (const float2*)grad_field, cam.grid_x, p0, acc, rec); break;
-      }
-      CVHRF_LAUNCH_CHECK();
+    CVHRF_CUDA_TRY(cudaMemsetAsync(rec, 0, (size_t)num_pairs * (6 + s.K + 2 * s.C) * sizeof(float), st));
+    const int2* rg = (const int2*)ranges;
+    const float2* gf = (const float2*)grad_field;
+#define CVHRF_BWD(CC)                                                                                       \
+  render_backward_kernel<CC><<<grid, 128, 0, st>>>(rg, pl, b.slot, g.rec0, g.cov2d, s.colours, s.phase,      \
+                                                   s.plane_probs, final_Ts, n_contrib, gf, s.K, s.W, s.H,    \
+                                                   cam.grid_x, rec)
+    switch (s.C) {
+      case 1: CVHRF_BWD(1); break;
+      case 2: CVHRF_BWD(2); break;
+      default: CVHRF_BWD(3); break;
     }
+#undef CVHRF_BWD
+    CVHRF_LAUNCH_CHECK();
   }
   gaussian_grad_kernel<<<(s.N + 127) / 128, 128, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
                                                           grad_scales, grad_colours, grad_phase, grad_opacities,
