@@ -41,6 +41,10 @@ SIGNATURES = {
     "cvhrf_raster_backward_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cvhrf_raster_backward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 9),
+    "cvhrf_scene_workspace_bytes": (c_size_t, [c_int]),
+    "cvhrf_scene_prepare": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_float, c_void_p, c_size_t]
+                            + [c_void_p] * 9 + [c_void_p]),
+    "cvhrf_scene_backward": (c_int, [c_void_p, c_void_p, c_void_p] + [c_void_p] * 14 + [c_void_p]),
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
 }
 
@@ -49,6 +53,13 @@ class AdamGroup(ctypes.Structure):
     """cvhrf_adam_group (include/cvhrf.h)."""
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
                 ("N", c_int), ("D", c_int), ("dense", c_int), ("lr", c_float), ("eps", c_float)]
+
+
+class Gaussians(ctypes.Structure):
+    """cvhrf_gaussians (include/cvhrf.h)."""
+    _fields_ = [("N", c_int), ("K", c_int), ("C", c_int)] + \
+               [(n, c_void_p) for n in ("means", "pre_quats", "pre_scales", "colours", "pre_phase", "pre_opac",
+                                        "pre_planes")]
 
 
 class RasterScene(ctypes.Structure):

@@ -71,12 +71,15 @@ struct BwdG {
   float E, G;
 };
 
-// Per-pixel state of one plane's back-to-front replay (backward_splat.cu:133-148).
+// Per-pixel state of one plane's back-to-front replay (backward_splat.cu:133-148).  The
+// reference updates the accumulated colour lazily, at the next contributor, from the
+// previous contributor's alpha and colour; applying that same update right after each
+// contributor gives identical values and needs no last-alpha / last-colour registers.
 template <int C>
 struct PixState {
-  float T, la;                    // transmittance, last alpha
+  float T;                        // transmittance
   int last;                       // n_contrib: positions >= last are skipped
-  float2 dL[C], acc[C], lc[C];    // dL/dpixel, accumulated colour, last colour
+  float2 dL[C], acc[C];           // dL/dpixel, accumulated colour behind
 };
 
 // One pixel, one Gaussian: renderBackwardTileKernel's arithmetic (:184-300), adding this
@@ -92,21 +95,19 @@ __device__ __forceinline__ void bwd_pixel(PixState<C>& st, const BwdG& g, float 
   if (alpha < 1.0f / 255.0f) return;
   st.T = st.T / (1.0f - alpha);
   const float dch = alpha * st.T;
-  const float2 la2 = make_float2(st.la, st.la);
-  const float2 nla2 = make_float2(1.0f - st.la, 1.0f - st.la);
+  const float2 a2 = make_float2(alpha, alpha);
+  const float2 na2 = make_float2(1.0f - alpha, 1.0f - alpha);
   float dL_dalpha = 0.0f;
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    st.acc[c] = __ffma2_rn(la2, st.lc[c], __fmul2_rn(nla2, st.acc[c]));
-    st.lc[c] = cpx[c];
     const float2 t = __fmul2_rn(__fadd2_rn(cpx[c], make_float2(-st.acc[c].x, -st.acc[c].y)), st.dL[c]);
     dL_dalpha += t.x;
     dL_dalpha += t.y;
     v[7 + c] += dch * (cs[c].x * st.dL[c].x + cs[c].y * st.dL[c].y);
     v[7 + C + c] += dch * (-cpx[c].y * st.dL[c].x + cpx[c].x * st.dL[c].y);
+    st.acc[c] = __ffma2_rn(a2, cpx[c], __fmul2_rn(na2, st.acc[c]));
   }
   dL_dalpha *= st.T;
-  st.la = alpha;
   const float dL_dG = g.opacity * w * dL_dalpha;
   const float gdx = G * d.x, gdy = G * d.y;
   v[0] += dL_dG * (-gdx * g.cx - gdy * g.cy) * ddelx_dx;
@@ -128,7 +129,7 @@ __device__ __forceinline__ void bwd_pixel(PixState<C>& st, const BwdG& g, float 
 // for each of those reduces the per-pixel contributions over the CTA into the pair's
 // record (records start at zero; each pass adds its plane's share).
 template <int C>
-__global__ void __launch_bounds__(128, 3) render_backward_kernel(
+__global__ void __launch_bounds__(128, 4) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
     const float4* __restrict__ rec0, const float4* __restrict__ cov2d, const float* __restrict__ colours,
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
@@ -169,12 +170,11 @@ __global__ void __launch_bounds__(128, 3) render_backward_kernel(
     s1.T = in1 ? final_T[p * HW + pix1] : 0.f;
     s0.last = in0 ? n_contrib[p * HW + pix0] : 0;
     s1.last = in1 ? n_contrib[p * HW + pix1] : 0;
-    s0.la = s1.la = 0.f;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
       s0.dL[c] = in0 ? grad_field[(size_t)(p * C + c) * HW + pix0] : make_float2(0.f, 0.f);
       s1.dL[c] = in1 ? grad_field[(size_t)(p * C + c) * HW + pix1] : make_float2(0.f, 0.f);
-      s0.acc[c] = s1.acc[c] = s0.lc[c] = s1.lc[c] = make_float2(0.f, 0.f);
+      s0.acc[c] = s1.acc[c] = make_float2(0.f, 0.f);
     }
     __syncthreads();
     if (threadIdx.x == 0) s_maxlast = 0;

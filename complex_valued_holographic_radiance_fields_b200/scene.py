@@ -150,3 +150,70 @@ def splat_args(kw):
     return (kw["cam_means_3D"], kw["z_vals"], kw["quats"], kw["scales"], kw["colours"], kw["phase"],
             kw["opacities"], kw["plane_probs"], kw["fx"], kw["fy"], kw["px"], kw["py"], kw["view_matrix"],
             kw["img_size"], kw["near_plane"], kw["far_plane"])
+
+
+_PARAM_ORDER = ("means", "pre_act_quats", "pre_act_scales", "colours", "pre_act_phase", "pre_act_opacities",
+                "pre_act_plane_assignment")
+
+
+class FusedRenderInputs(torch.autograd.Function):
+    """`render_inputs` as two libcvhrf kernels (cvhrf_scene_prepare / cvhrf_scene_backward).
+
+    Returns the rasterizer inputs for ALL rows in depth order (rows outside near/far sort
+    last and are culled by the rasterizer) plus `order`, the parameter row of each.
+    """
+
+    @staticmethod
+    def forward(ctx, means, pq, ps, col, pph, pop, ppl, R, T, near, far):
+        import ctypes
+        from . import _lib
+        dev = means.device
+        ins = [t.contiguous() for t in (means, pq, ps, col, pph, pop, ppl)]
+        N, C, K = means.shape[0], col.shape[1], ppl.shape[1]
+        G = _lib.Gaussians(N, K, C, *[t.data_ptr() for t in ins])
+        R = R.to(dev, torch.float32).contiguous()
+        T = T.to(dev, torch.float32).contiguous()
+        L = _lib.lib()
+        ws = torch.empty(max(1, L.cvhrf_scene_workspace_bytes(N)), dtype=torch.uint8, device=dev)
+        f32 = dict(dtype=torch.float32, device=dev)
+        order = torch.empty(N, dtype=torch.int32, device=dev)
+        outs = [torch.empty(N, 3, **f32), torch.empty(N, **f32), torch.empty(N, 4, **f32), torch.empty(N, 3, **f32),
+                torch.empty(N, C, **f32), torch.empty(N, C, **f32), torch.empty(N, **f32), torch.empty(N, K, **f32)]
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(L.cvhrf_scene_prepare(ctypes.byref(G), R.data_ptr(), T.data_ptr(), float(near), float(far),
+                                         ws.data_ptr(), ws.numel(), order.data_ptr(),
+                                         *[o.data_ptr() for o in outs], st), "cvhrf_scene_prepare")
+        ctx.save_for_backward(*ins, R, order)
+        ctx.mark_non_differentiable(order, outs[1])
+        return (*outs, order)
+
+    @staticmethod
+    def backward(ctx, g_cam, g_z, g_q, g_s, g_col, g_ph, g_op, g_pl, g_order):
+        import ctypes
+        from . import _lib
+        *ins, R, order = ctx.saved_tensors
+        N, C, K = ins[0].shape[0], ins[3].shape[1], ins[6].shape[1]
+        dev = ins[0].device
+        G = _lib.Gaussians(N, K, C, *[t.data_ptr() for t in ins])
+
+        def g(t, shape):
+            return torch.zeros(shape, dtype=torch.float32, device=dev) if t is None else t.contiguous()
+        gs = [g(g_cam, (N, 3)), g(g_q, (N, 4)), g(g_s, (N, 3)), g(g_col, (N, C)), g(g_ph, (N, C)), g(g_op, (N,)),
+              g(g_pl, (N, K))]
+        d = [torch.empty_like(t) for t in ins]
+        st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(_lib.lib().cvhrf_scene_backward(ctypes.byref(G), R.data_ptr(), order.data_ptr(),
+                                                     *[t.data_ptr() for t in gs], *[t.data_ptr() for t in d], st),
+                   "cvhrf_scene_backward")
+        return (*d, None, None, None, None)
+
+
+def render_inputs_fused(params, camera):
+    """Same contract as `render_inputs`, through the fused kernels (all rows, culled by depth)."""
+    outs = FusedRenderInputs.apply(*[params[k] for k in _PARAM_ORDER], camera.R, camera.T, camera.near, camera.far)
+    cam, z, q, s, col, ph, op, pl, order = outs
+    kw = dict(cam_means_3D=cam, z_vals=z, quats=q, scales=s, colours=col, phase=ph, opacities=op, plane_probs=pl,
+              fx=camera.fx, fy=camera.fy, px=camera.px, py=camera.py,
+              view_matrix=camera.R.to(params["means"].device, torch.float32).contiguous(),
+              img_size=(camera.W, camera.H), near_plane=camera.near, far_plane=camera.far)
+    return kw, order.long()

@@ -52,7 +52,7 @@ class HoloTrainer:
         self.target = target.to(self.device)
 
     def forward(self, target=None):
-        kw, idxs = SC.render_inputs(self.params, self.camera)
+        kw, idxs = SC.render_inputs_fused(self.params, self.camera)
         field, visible = splat_tile_cuda(*SC.splat_args(kw))
         holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
         tgt = self.target if target is None else target

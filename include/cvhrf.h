@@ -214,6 +214,44 @@ typedef struct {
 int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, const int64_t* visible, int V,
                       float beta1, float beta2, void* stream);
 
+/* ---- caller glue: filter, depth sort, gather, activations ---------------------- */
+/*
+ * Pre-activation Gaussian parameters as the model stores them (model.py:138-169):
+ * means N x 3, pre_quats N x 4, pre_scales N x 3 (log scales), colours N x C,
+ * pre_phase N x C, pre_opac N, pre_planes N x K (plane logits); float32, device.
+ */
+typedef struct {
+  int N, K, C;
+  const float* means;
+  const float* pre_quats;
+  const float* pre_scales;
+  const float* colours;
+  const float* pre_phase;
+  const float* pre_opac;
+  const float* pre_planes;
+} cvhrf_gaussians;
+
+/*
+ * Scene.render up to the splat call (model.py:1365-1402 with apply_activations
+ * :595-608 and the straight-through one-hot :41-56), fused: X_cam = X R + T (R 3x3
+ * row-major, T 3; device), depth sort of the rows with near < z < far (rows outside
+ * sort last and keep their out-of-range depth, so the rasterizer culls them), gather
+ * and activation.  Outputs are the N rows in that order (the rasterizer's inputs);
+ * order[s] is the parameter row of sorted row s.  No host synchronisation.
+ */
+size_t cvhrf_scene_workspace_bytes(int N);
+int cvhrf_scene_prepare(const cvhrf_gaussians* gaussians, const float* R, const float* T, float near_plane,
+                        float far_plane, void* workspace, size_t workspace_bytes, int32_t* order,
+                        float* cam_means, float* z_vals, float* quats, float* scales, float* colours,
+                        float* phase, float* opacities, float* plane_probs, void* stream);
+/* Backward of cvhrf_scene_prepare: gradients of the sorted rows -> parameter rows (every row written). */
+int cvhrf_scene_backward(const cvhrf_gaussians* gaussians, const float* R, const int32_t* order,
+                         const float* g_cam_means, const float* g_quats, const float* g_scales,
+                         const float* g_colours, const float* g_phase, const float* g_opacities,
+                         const float* g_plane_probs, float* d_means, float* d_pre_quats, float* d_pre_scales,
+                         float* d_colours, float* d_pre_phase, float* d_pre_opacities, float* d_pre_planes,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif
