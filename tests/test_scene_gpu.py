@@ -34,4 +34,7 @@ def test_fused_glue_matches_torch(cuda, N, K, C, view):
     la.backward()
     lb.backward()
     for k in pa:
-        assert torch.allclose(pa[k].grad, pb[k].grad, rtol=1e-4, atol=1e-5), k
+        # the straight-through gradient is softmax(x / 0.001) with logits ~1e4: one ulp of a
+        # scaled logit moves exp() by ~1e-3 relative, so it is compared at 1e-3
+        rtol = 1e-3 if k == "pre_act_plane_assignment" else 1e-4
+        assert torch.allclose(pa[k].grad, pb[k].grad, rtol=rtol, atol=1e-5), k
