@@ -109,11 +109,11 @@ def peaks():
 
 
 def propagation_bytes(K, C, H, W, S):
-    """HBM bytes the three-pass fused propagation moves per forward call (the kernels as built):
-    rows: read K C H W, write K C H P; columns: read K C H P, write C S P once + (K-1) RMW of C S P;
-    inverse rows: read C S P, write C S S  (complex64 = 8 B)."""
+    """Algorithmic HBM bytes of one fused multi-plane propagation forward (the kernels as built):
+    rows: read K C H W, write K C H P; columns (K planes summed on chip): read K C H P, write C S P;
+    inverse rows: read C S P, write C S S  (complex64 = 8 B, P = 2 S)."""
     P = 2 * S
-    return 8 * (K * C * H * W + 2 * K * C * H * P + C * S * P * (1 + 2 * (K - 1)) + C * S * P + C * S * S)
+    return 8 * (K * C * H * W + 2 * K * C * H * P + 2 * C * S * P + C * S * S)
 
 
 def run_mine(args, world, rank, local):

@@ -24,17 +24,9 @@
 #include <vector>
 #include "common.cuh"
 #include "fft_lines.cuh"
+#include "asm_static.cuh"
 
 namespace cvhrf {
-
-struct TransferParams {
-  float k;          // (float)(2 pi / lambda), computed in double as the reference host code does
-  float distance;
-  float fx_max, fy_max;
-  float inv_np;     // (float)(1 / (P * pitch)): torch.fft.fftfreq scale
-  float aperture;   // radius in shifted index space; <= 0 disables
-  float offset_x, offset_y;
-};
 
 // Per-launch list of column jobs (one job = one input spectrum item -> one output item).
 constexpr int kMaxJobs = 32;
@@ -44,58 +36,6 @@ struct ColumnJobs {
   int out_item[kMaxJobs];
   TransferParams tp[kMaxJobs];
 };
-
-// Host-side constants of bandlimited_propagation_cuda.cu:149-170 (float arithmetic,
-// k via double), for a square padded grid of side P.
-static TransferParams make_transfer(float wavelength, float pitch, float distance, float aperture, int P) {
-  TransferParams t;
-  t.k = (float)(2.0f * M_PI / wavelength);
-  const float x_size = pitch * P;
-  const float y_size = pitch * P;
-  const float ax = 2.0f * distance * (1.0f / x_size);
-  const float ay = 2.0f * distance * (1.0f / y_size);
-  t.fx_max = 1.0f / sqrtf(ax * ax + 1.0f) / wavelength;
-  t.fy_max = 1.0f / sqrtf(ay * ay + 1.0f) / wavelength;
-  t.distance = distance;
-  t.inv_np = (float)(1.0 / ((double)P * (double)pitch));
-  t.aperture = aperture;
-  t.offset_x = P / 2.0f - 0.5f;
-  t.offset_y = P / 2.0f - 0.5f;
-  return t;
-}
-
-// Transfer function x aperture at unshifted bin (ku = row, kv = column) of a P x P
-// grid.  Row bins carry FX (meshgrid 'ij', python_function.py:137-142), column bins FY.
-// The expressions follow bandlimited_propagation_cuda.cu:50-85 term by term (kz^2 in
-// double, stored to float, sqrtf, phase = d*kz, accurate sincosf); the aperture test is
-// on shifted indices (i + P/2) mod P.
-__device__ __forceinline__ float2 transfer_at(int ku, int kv, int P, const TransferParams& tp) {
-  const int half = P >> 1;
-  const float fx_val = __fmul_rn((float)(ku < half ? ku : ku - P), tp.inv_np);
-  const float fy_val = __fmul_rn((float)(kv < half ? kv : kv - P), tp.inv_np);
-  const bool within_bandlimit = (fabsf(fx_val) < tp.fx_max) && (fabsf(fy_val) < tp.fy_max);
-  const float k = tp.k;
-  const float kz_squared = k * k - (2 * M_PI * fx_val) * (2 * M_PI * fx_val) - (2 * M_PI * fy_val) * (2 * M_PI * fy_val);
-  float2 tr = make_float2(0.0f, 0.0f);
-  if (kz_squared > 0.0f && within_bandlimit) {
-    const float kz = sqrtf(kz_squared);
-    const float phase = tp.distance * kz;
-    float s, c;
-    sincosf(phase, &s, &c);
-    tr = make_float2(c, s);
-  }
-  if (tp.aperture > 0.0f) {
-    const int idx = (kv + half) % P;  // shifted column index
-    const int idy = (ku + half) % P;  // shifted row index
-    const float x = (float)idx - tp.offset_x;
-    const float y = (float)idy - tp.offset_y;
-    const float r = tp.aperture;
-    const float m = (x * x + y * y < r * r) ? 1.0f : 0.0f;
-    tr.x *= m;
-    tr.y *= m;
-  }
-  return tr;
-}
 
 // ---- pass A: forward row transforms ------------------------------------------------
 // in: items x Hi x Wi; A: items x Hi x P, each row in split digit-reversed bin order
@@ -267,14 +207,22 @@ extern "C" int cvhrf_asm_plan_create(int S, cvhrf_asm_plan** plan_out) {
     double a = -2.0 * M_PI * (double)t / (double)P;
     twP[t] = make_float2((float)cos(a), (float)sin(a));
   }
-  // digit reversal: bin k = m1 + R1 (m2 + R2 (...)) sits at position sum_i L_i m_i
+  // digit reversal: bin k = m1 + R1 (m2 + R2 (...)) sits at position sum_i L_i m_i, for the
+  // stage radices of the plan that will run (the compile-time plan where one exists)
+  int rad[kMaxFftStages], Ls[kMaxFftStages], nst = d.nst;
+  for (int i = 0; i < d.nst; ++i) { rad[i] = d.radix[i]; Ls[i] = d.L[i]; }
+  if (static_fft_size(S)) {
+    static_fft_radices(S, rad, &nst);
+    int L = S;
+    for (int i = 0; i < nst; ++i) { L /= rad[i]; Ls[i] = L; }
+  }
   std::vector<int> digrev(S);
   for (int k = 0; k < S; ++k) {
     int rem = k, pos = 0;
-    for (int i = 0; i < d.nst; ++i) {
-      int m = rem % d.radix[i];
-      rem /= d.radix[i];
-      pos += d.L[i] * m;
+    for (int i = 0; i < nst; ++i) {
+      int m = rem % rad[i];
+      rem /= rad[i];
+      pos += Ls[i] * m;
     }
     digrev[pos] = k;
   }
@@ -376,6 +324,14 @@ extern "C" int cvhrf_asm_propagate(const cvhrf_asm_plan* plan, const void* in, i
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
+  if (static_fft_size(d.S)) {
+    SumJobs sj{};
+    sj.nin[0] = 1;
+    sj.tp[0][0] = make_transfer(wavelength, pixel_pitch, distance, aperture, P);
+    if ((rc = static_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
+    if ((rc = static_columns(d, A, Hi, B, Ho, sj, 1, st))) return rc;
+    return static_rows_inverse(d, B, Ho, (float2*)out, Wo, accumulate, st);
+  }
   if ((rc = launch_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
   ColumnJobs jobs{};
   jobs.n = 1;
@@ -400,6 +356,21 @@ extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
+  if (static_fft_size(d.S) && K <= kMaxSumInputs) {
+    SumJobs sj{};
+    for (int c = 0; c < C; ++c) {
+      if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+      sj.nin[c] = K;
+      sj.out_item[c] = c;
+      for (int p = 0; p < K; ++p) {
+        sj.in_item[c][p] = p * C + c;
+        sj.tp[c][p] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
+      }
+    }
+    if ((rc = static_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
+    if ((rc = static_columns(d, A, H, B, S, sj, C, st))) return rc;
+    return static_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+  }
   if ((rc = launch_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
   for (int p = 0; p < K; ++p) {
     ColumnJobs jobs{};
@@ -429,6 +400,20 @@ extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, co
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
+  if (static_fft_size(d.S)) {
+    SumJobs sj{};
+    for (int p = 0; p < K; ++p)
+      for (int c = 0; c < C; ++c) {
+        if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+        sj.nin[p * C + c] = 1;
+        sj.out_item[p * C + c] = p * C + c;
+        sj.in_item[p * C + c][0] = c;
+        sj.tp[p * C + c][0] = make_transfer(wavelengths[c], pixel_pitch, -distances[p], aperture, P);
+      }
+    if ((rc = static_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
+    if ((rc = static_columns(d, A, S, B, H, sj, K * C, st))) return rc;
+    return static_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+  }
   if ((rc = launch_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
   ColumnJobs jobs{};
   jobs.n = K * C;

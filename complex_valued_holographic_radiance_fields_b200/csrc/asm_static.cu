@@ -1,0 +1,247 @@
+// Propagation passes specialised for compile-time line lengths (see fft_static.cuh).
+//
+// Same three-pass algorithm and arithmetic as asm_propagation.cu (rows forward; columns
+// with the transfer function; rows inverse with crop), with two differences:
+//   * the FFTs use StaticPlan<S> (composite radices <= 32 in registers);
+//   * the column pass sums several inputs (the K planes of one channel, each with its own
+//     transfer function) into one output in shared memory, so a multi-plane propagation
+//     writes the intermediate once instead of read-modify-writing it per plane.
+#include "asm_static.cuh"
+#include "fft_static.cuh"
+
+namespace cvhrf {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int S>
+__global__ void __launch_bounds__(kThreads) rows_forward_s(const float2* __restrict__ in, int total_rows, int Wi,
+                                                          float2* __restrict__ A, const float2* __restrict__ tw,
+                                                          const float2* __restrict__ twP, int rows) {
+  extern __shared__ float2 sm[];
+  constexpr int P = 2 * S;
+  const int ow = (P - Wi) / 2;
+  const int row0 = blockIdx.x * rows;
+  const int nrows = min(rows, total_rows - row0);
+  if (nrows <= 0) return;
+  for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
+    const int r = e / S, t = e - r * S;
+    const float2* src = in + (size_t)(row0 + r) * Wi;
+    int pos = t;
+    int j = pos - ow;
+    if (j < 0 || j >= Wi) { pos = t + S; j = pos - ow; }
+    float2 v = make_float2(0.f, 0.f), vo = v;
+    if (j >= 0 && j < Wi) {
+      v = src[j];
+      vo = cmul(v, __ldg(&twP[pos]));
+    }
+    sm[(2 * r) * S + t] = v;
+    sm[(2 * r + 1) * S + t] = vo;
+  }
+  __syncthreads();
+  static_fft_forward<S>(sm, 2 * nrows, S, tw);
+  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
+    const int r = e / P, q = e - r * P;
+    A[(size_t)(row0 + r) * P + q] = sm[(2 * r) * S + q];
+  }
+}
+
+template <int S>
+__global__ void __launch_bounds__(kThreads) columns_s(const float2* __restrict__ A, int Hi, float2* __restrict__ B,
+                                                     int Ho, const float2* __restrict__ tw,
+                                                     const float2* __restrict__ twP, const int* __restrict__ digrev,
+                                                     int cols, const SumJobs jobs) {
+  extern __shared__ float2 sm[];
+  constexpr int P = 2 * S;
+  const int job = blockIdx.y;
+  const int q0 = blockIdx.x * cols;
+  const int ncols = min(cols, P - q0);
+  float2* acc = sm + 2 * cols * S;  // Ho x ncols output accumulator
+  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
+  const int nin = jobs.nin[job];
+  for (int k = 0; k < nin; ++k) {
+    const float2* Ain = A + (size_t)jobs.in_item[job][k] * Hi * P;
+    const TransferParams tp = jobs.tp[job][k];
+    for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+      const int t = e / ncols, c = e - t * ncols;
+      int pos = t;
+      int r = pos - oh;
+      if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
+      float2 v = make_float2(0.f, 0.f), vo = v;
+      if (r >= 0 && r < Hi) {
+        v = Ain[(size_t)r * P + q0 + c];
+        vo = cmul(v, __ldg(&twP[pos]));
+      }
+      sm[(2 * c) * S + t] = v;
+      sm[(2 * c + 1) * S + t] = vo;
+    }
+    __syncthreads();
+    static_fft_forward<S>(sm, 2 * ncols, S, tw);
+    for (int e = threadIdx.x; e < 2 * ncols * S; e += blockDim.x) {
+      const int line = e / S, pos = e - line * S;
+      const int c = line >> 1, h = line & 1;
+      const int q = q0 + c;
+      const int qh = q >= S ? 1 : 0;
+      const int kv = 2 * __ldg(&digrev[q - qh * S]) + qh;
+      const int ku = 2 * __ldg(&digrev[pos]) + h;
+      sm[e] = cmul(sm[e], transfer_at(ku, kv, P, tp));
+    }
+    __syncthreads();
+    static_fft_inverse<S>(sm, 2 * ncols, S, tw);
+    for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+      const int rr = e / ncols, c = e - rr * ncols;
+      const int n = oc + rr;
+      const int t = n >= S ? n - S : n;
+      const float2 v = cadd(sm[(2 * c) * S + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * c + 1) * S + t]));
+      acc[e] = k == 0 ? v : cadd(acc[e], v);
+    }
+    __syncthreads();
+  }
+  float2* Bout = B + (size_t)jobs.out_item[job] * Ho * P;
+  for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+    const int rr = e / ncols, c = e - rr * ncols;
+    Bout[(size_t)rr * P + q0 + c] = acc[e];
+  }
+}
+
+template <int S>
+__global__ void __launch_bounds__(kThreads) rows_inverse_s(const float2* __restrict__ B, int total_rows,
+                                                          float2* __restrict__ out, int Wo,
+                                                          const float2* __restrict__ tw,
+                                                          const float2* __restrict__ twP, int rows, float scale,
+                                                          int accumulate) {
+  extern __shared__ float2 sm[];
+  constexpr int P = 2 * S;
+  const int row0 = blockIdx.x * rows;
+  const int nrows = min(rows, total_rows - row0);
+  if (nrows <= 0) return;
+  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
+    const int r = e / P, q = e - r * P;
+    sm[(2 * r) * S + q] = B[(size_t)(row0 + r) * P + q];
+  }
+  __syncthreads();
+  static_fft_inverse<S>(sm, 2 * nrows, S, tw);
+  const int oc = (P - Wo) / 2;
+  for (int e = threadIdx.x; e < nrows * Wo; e += blockDim.x) {
+    const int r = e / Wo, x = e - r * Wo;
+    const int n = oc + x;
+    const int t = n >= S ? n - S : n;
+    float2 v = cadd(sm[(2 * r) * S + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * r + 1) * S + t]));
+    v.x *= scale;
+    v.y *= scale;
+    float2* dst = out + (size_t)(row0 + r) * Wo + x;
+    if (accumulate) v = cadd(*dst, v);
+    *dst = v;
+  }
+}
+
+constexpr size_t kStaticSmem = 64 * 1024;
+
+template <int S>
+int static_lines(size_t extra_per_line, size_t budget = kStaticSmem) {
+  const size_t per = 2 * (size_t)S * sizeof(float2) + extra_per_line;
+  int r = (int)(budget / per);
+  int p2 = 1;
+  while (p2 * 2 <= r && p2 < 8) p2 *= 2;
+  return p2;
+}
+
+template <int S>
+int run_rows_forward(const float2* in, int total_rows, int Wi, float2* A, const float2* tw, const float2* twP,
+                     cudaStream_t st) {
+  const int rows = static_lines<S>(0);
+  const size_t smem = (size_t)rows * 2 * S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_forward_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rows_forward_s<S><<<(total_rows + rows - 1) / rows, kThreads, smem, st>>>(in, total_rows, Wi, A, tw, twP, rows);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+template <int S>
+int run_columns(const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP, const int* digrev,
+                const SumJobs& jobs, int njobs, cudaStream_t st) {
+  const int cols = static_lines<S>((size_t)S * sizeof(float2), 100 * 1024);  // + Ho x cols accumulator (Ho <= S)
+  const size_t smem = (size_t)cols * 2 * S * sizeof(float2) + (size_t)cols * S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((2 * S + cols - 1) / cols, njobs);
+  columns_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, digrev, cols, jobs);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+template <int S>
+int run_rows_inverse(const float2* B, int total_rows, float2* out, int Wo, const float2* tw, const float2* twP,
+                     int accumulate, cudaStream_t st) {
+  const int rows = static_lines<S>(0);
+  const size_t smem = (size_t)rows * 2 * S * sizeof(float2);
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_inverse_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const float P = 2.0f * S;
+  rows_inverse_s<S><<<(total_rows + rows - 1) / rows, kThreads, smem, st>>>(B, total_rows, out, Wo, tw, twP, rows,
+                                                                            1.0f / (P * P), accumulate);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+}  // namespace
+
+bool static_fft_size(int S) {
+  switch (S) {
+    case 64: case 128: case 256: case 384: case 512: case 800: case 1024: case 1920: case 2048: return true;
+    default: return false;
+  }
+}
+
+void static_fft_radices(int S, int* radix, int* nst) {
+#define CVHRF_PLAN(SS) \
+  case SS: radix[0] = StaticPlan<SS>::r0; radix[1] = StaticPlan<SS>::r1; radix[2] = StaticPlan<SS>::r2; \
+    *nst = StaticPlan<SS>::nst; break;
+  switch (S) {
+    CVHRF_PLAN(64) CVHRF_PLAN(128) CVHRF_PLAN(256) CVHRF_PLAN(384) CVHRF_PLAN(512) CVHRF_PLAN(800)
+    CVHRF_PLAN(1024) CVHRF_PLAN(1920) CVHRF_PLAN(2048)
+    default: *nst = 0;
+  }
+#undef CVHRF_PLAN
+}
+
+int static_rows_forward(const FftDesc& d, const float2* in, int total_rows, int Wi, float2* A, cudaStream_t st) {
+#define CALL run_rows_forward
+#define ARGS (in, total_rows, Wi, A, d.tw, d.twP, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+int static_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho, const SumJobs& jobs, int njobs,
+                   cudaStream_t st) {
+#define CALL run_columns
+#define ARGS (A, Hi, B, Ho, d.tw, d.twP, d.digrev, jobs, njobs, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float2* out, int Wo, int accumulate,
+                        cudaStream_t st) {
+#define CALL run_rows_inverse
+#define ARGS (B, total_rows, out, Wo, d.tw, d.twP, accumulate, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+}  // namespace cvhrf

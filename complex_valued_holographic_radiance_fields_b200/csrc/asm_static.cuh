@@ -1,0 +1,91 @@
+// Shared pieces of the propagation passes: transfer-function constants and evaluation,
+// and the compile-time-size (static) pass entry points of asm_static.cu.
+#pragma once
+#include <math.h>
+#include "fft_lines.cuh"
+
+namespace cvhrf {
+
+struct TransferParams {
+  float k;          // (float)(2 pi / lambda), computed in double as the reference host code does
+  float distance;
+  float fx_max, fy_max;
+  float inv_np;     // (float)(1 / (P * pitch)): torch.fft.fftfreq scale
+  float aperture;   // radius in shifted index space; <= 0 disables
+  float offset_x, offset_y;
+};
+
+// Host-side constants of bandlimited_propagation_cuda.cu:149-170 (float arithmetic,
+// k via double), for a square padded grid of side P.
+inline TransferParams make_transfer(float wavelength, float pitch, float distance, float aperture, int P) {
+  TransferParams t;
+  t.k = (float)(2.0f * M_PI / wavelength);
+  const float x_size = pitch * P;
+  const float y_size = pitch * P;
+  const float ax = 2.0f * distance * (1.0f / x_size);
+  const float ay = 2.0f * distance * (1.0f / y_size);
+  t.fx_max = 1.0f / sqrtf(ax * ax + 1.0f) / wavelength;
+  t.fy_max = 1.0f / sqrtf(ay * ay + 1.0f) / wavelength;
+  t.distance = distance;
+  t.inv_np = (float)(1.0 / ((double)P * (double)pitch));
+  t.aperture = aperture;
+  t.offset_x = P / 2.0f - 0.5f;
+  t.offset_y = P / 2.0f - 0.5f;
+  return t;
+}
+
+// Transfer function x aperture at unshifted bin (ku = row, kv = column) of a P x P
+// grid.  Row bins carry FX (meshgrid 'ij', python_function.py:137-142), column bins FY.
+// The expressions follow bandlimited_propagation_cuda.cu:50-85 term by term (kz^2 in
+// double, stored to float, sqrtf, phase = d*kz, accurate sincosf); the aperture test is
+// on shifted indices (i + P/2) mod P.
+__device__ __forceinline__ float2 transfer_at(int ku, int kv, int P, const TransferParams& tp) {
+  const int half = P >> 1;
+  const float fx_val = __fmul_rn((float)(ku < half ? ku : ku - P), tp.inv_np);
+  const float fy_val = __fmul_rn((float)(kv < half ? kv : kv - P), tp.inv_np);
+  const bool within_bandlimit = (fabsf(fx_val) < tp.fx_max) && (fabsf(fy_val) < tp.fy_max);
+  const float k = tp.k;
+  const float kz_squared = k * k - (2 * M_PI * fx_val) * (2 * M_PI * fx_val) - (2 * M_PI * fy_val) * (2 * M_PI * fy_val);
+  float2 tr = make_float2(0.0f, 0.0f);
+  if (kz_squared > 0.0f && within_bandlimit) {
+    const float kz = sqrtf(kz_squared);
+    const float phase = tp.distance * kz;
+    float s, c;
+    sincosf(phase, &s, &c);
+    tr = make_float2(c, s);
+  }
+  if (tp.aperture > 0.0f) {
+    const int idx = (kv + half) % P;  // shifted column index
+    const int idy = (ku + half) % P;  // shifted row index
+    const float x = (float)idx - tp.offset_x;
+    const float y = (float)idy - tp.offset_y;
+    const float r = tp.aperture;
+    const float m = (x * x + y * y < r * r) ? 1.0f : 0.0f;
+    tr.x *= m;
+    tr.y *= m;
+  }
+  return tr;
+}
+
+// Column jobs of the static passes: output item out_item[j] = sum over k < nin[j] of the
+// propagation of input item in_item[j][k] with transfer function tp[j][k].
+constexpr int kMaxSumJobs = 32;
+constexpr int kMaxSumInputs = 8;
+struct SumJobs {
+  int nin[kMaxSumJobs];
+  int out_item[kMaxSumJobs];
+  int in_item[kMaxSumJobs][kMaxSumInputs];
+  TransferParams tp[kMaxSumJobs][kMaxSumInputs];
+};
+
+// Sizes with a compile-time plan (the rest use the runtime plan of asm_propagation.cu).
+bool static_fft_size(int S);
+// Stage radices of the static plan (radix[0..2], *nst stages) for the digit-reversal table.
+void static_fft_radices(int S, int* radix, int* nst);
+int static_rows_forward(const FftDesc& d, const float2* in, int total_rows, int Wi, float2* A, cudaStream_t st);
+int static_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho, const SumJobs& jobs, int njobs,
+                   cudaStream_t st);
+int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float2* out, int Wo, int accumulate,
+                        cudaStream_t st);
+
+}  // namespace cvhrf
