@@ -99,6 +99,14 @@ def fp32_peak_tflops(sm_mhz):
     return props.multi_processor_count * 128 * 2 * sm_mhz * 1e6 / 1e12
 
 
+# arithmetic of the reference's per-(pixel, Gaussian) backward body (backward_splat.cu:184-300)
+# for C = 3, counted once: power 6, alpha 3, T 2, 3 channels x 21, alpha/geometry/conic/cov 36
+BWD_FLOP_PER_EVAL = 110
+# dram__bytes_read.sum + dram__bytes_write.sum of render_backward_kernel<3> at this workload
+# (profiles/ncu_hot_kernels_config3_train_step.md)
+BWD_NCU_TRAFFIC = 298.1e6
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -128,6 +136,8 @@ def run_mine(args, world, rank, local):
     cam = SC.look_at_camera(IMG, IMG, 2 * math.pi * rank / max(world, 1), 0.0) if world > 1 else None
     tr = HoloTrainer(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES, device=dev, camera=cam)
     step = (lambda t=None: dp_step(tr, t)) if world > 1 else (lambda t=None: tr.step(t))
+    sampler = ClockSampler(local)   # sampling starts with the warm-up so the loaded period is covered
+    sampler.__enter__()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -141,8 +151,7 @@ def run_mine(args, world, rank, local):
     # --- device-timed region: inputs resident in HBM ---
     barrier()
     launches0 = L.cvhrf_kernel_launch_count()
-    sampler = ClockSampler(local)
-    with sampler, op_timing() as ops:
+    with op_timing() as ops:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -150,6 +159,7 @@ def run_mine(args, world, rank, local):
             loss = step()
         t1.record()
         barrier()
+    sampler.__exit__()
     launches = L.cvhrf_kernel_launch_count() - launches0
     ms = t0.elapsed_time(t1) / args.steps
     opsum = ops.summary()
@@ -187,6 +197,19 @@ def run_mine(args, world, rank, local):
                  "achieved": pbytes / (prop_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
                  "peak_source": hbm_src, "algorithmic_bytes": pbytes, "traffic": None}
     roof_prop["frac"] = roof_prop["achieved"] / hbm
+    # dominant operator: the rasterizer backward, bound by the FP32 pipe (not HBM, not tensor cores)
+    from complex_valued_holographic_radiance_fields_b200 import rasterizer as RZ
+    evals = 256.0 * RZ.last_num_pairs          # pixel x (tile, Gaussian) pair evaluations, one plane each
+    bwd_ms = opsum.get("raster_backward", (1, float("nan")))[1]
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    peak_tf = fp32_peak_tflops(sm_mhz)
+    roof = {"op": "raster_backward (render_backward_kernel + gaussian_grad_kernel)", "bound": "fp32",
+            "achieved": evals * BWD_FLOP_PER_EVAL / (bwd_ms * 1e-3) / 1e12, "peak": peak_tf, "unit": "TFLOP/s",
+            "peak_source": f"SMs x 128 FMA lanes x 2 x median SM clock {sm_mhz:.0f} MHz (no tensor-core work)",
+            "algorithmic_flop": evals * BWD_FLOP_PER_EVAL,
+            "work_unit": f"{BWD_FLOP_PER_EVAL} FLOP per pixel-pair evaluation x 256 x {RZ.last_num_pairs} pairs",
+            "traffic": BWD_NCU_TRAFFIC}
+    roof["frac"] = roof["achieved"] / peak_tf
     line = {
         "metric": METRIC, "value": world * 1000.0 / ms_max, "unit": "iters/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
@@ -197,7 +220,8 @@ def run_mine(args, world, rank, local):
         "gpu_launches": int(launches),
         "ops_ms": {k: round(v[1], 4) for k, v in opsum.items()},
         "dominant_op": dom[0],
-        "roofline": roof_prop,
+        "roofline": roof,
+        "roofline_propagation": roof_prop,
         "clocks": clocks,
         "loss": float(loss.item()),
     }

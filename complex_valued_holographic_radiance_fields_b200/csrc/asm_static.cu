@@ -53,15 +53,17 @@ __global__ void __launch_bounds__(kThreads) columns_s(const float2* __restrict__
                                                      int cols, const SumJobs jobs) {
   extern __shared__ float2 sm[];
   constexpr int P = 2 * S;
+  constexpr int LD = S + 1;  // padded line stride: consecutive lines start in different banks
   const int job = blockIdx.y;
   const int q0 = blockIdx.x * cols;
   const int ncols = min(cols, P - q0);
-  float2* acc = sm + 2 * cols * S;  // Ho x ncols output accumulator
+  float2* acc = sm + 2 * cols * LD;  // Ho x ncols output accumulator
   const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
   const int nin = jobs.nin[job];
   for (int k = 0; k < nin; ++k) {
     const float2* Ain = A + (size_t)jobs.in_item[job][k] * Hi * P;
     const TransferParams tp = jobs.tp[job][k];
+#pragma unroll 4
     for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
       const int t = e / ncols, c = e - t * ncols;
       int pos = t;
@@ -72,11 +74,11 @@ __global__ void __launch_bounds__(kThreads) columns_s(const float2* __restrict__
         v = Ain[(size_t)r * P + q0 + c];
         vo = cmul(v, __ldg(&twP[pos]));
       }
-      sm[(2 * c) * S + t] = v;
-      sm[(2 * c + 1) * S + t] = vo;
+      sm[(2 * c) * LD + t] = v;
+      sm[(2 * c + 1) * LD + t] = vo;
     }
     __syncthreads();
-    static_fft_forward<S>(sm, 2 * ncols, S, tw);
+    static_fft_forward<S>(sm, 2 * ncols, LD, tw);
     for (int e = threadIdx.x; e < 2 * ncols * S; e += blockDim.x) {
       const int line = e / S, pos = e - line * S;
       const int c = line >> 1, h = line & 1;
@@ -84,15 +86,15 @@ __global__ void __launch_bounds__(kThreads) columns_s(const float2* __restrict__
       const int qh = q >= S ? 1 : 0;
       const int kv = 2 * __ldg(&digrev[q - qh * S]) + qh;
       const int ku = 2 * __ldg(&digrev[pos]) + h;
-      sm[e] = cmul(sm[e], transfer_at(ku, kv, P, tp));
+      sm[line * LD + pos] = cmul(sm[line * LD + pos], transfer_at(ku, kv, P, tp));
     }
     __syncthreads();
-    static_fft_inverse<S>(sm, 2 * ncols, S, tw);
+    static_fft_inverse<S>(sm, 2 * ncols, LD, tw);
     for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
       const int rr = e / ncols, c = e - rr * ncols;
       const int n = oc + rr;
       const int t = n >= S ? n - S : n;
-      const float2 v = cadd(sm[(2 * c) * S + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * c + 1) * S + t]));
+      const float2 v = cadd(sm[(2 * c) * LD + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * c + 1) * LD + t]));
       acc[e] = k == 0 ? v : cadd(acc[e], v);
     }
     __syncthreads();
@@ -160,8 +162,8 @@ int run_rows_forward(const float2* in, int total_rows, int Wi, float2* A, const 
 template <int S>
 int run_columns(const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP, const int* digrev,
                 const SumJobs& jobs, int njobs, cudaStream_t st) {
-  const int cols = static_lines<S>((size_t)S * sizeof(float2), 100 * 1024);  // + Ho x cols accumulator (Ho <= S)
-  const size_t smem = (size_t)cols * 2 * S * sizeof(float2) + (size_t)cols * S * sizeof(float2);
+  const int cols = static_lines<S>((size_t)S * sizeof(float2) + 16, 100 * 1024);  // + Ho x cols accumulator (Ho <= S)
+  const size_t smem = (size_t)cols * 2 * (S + 1) * sizeof(float2) + (size_t)cols * S * sizeof(float2);
   CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((2 * S + cols - 1) / cols, njobs);
   columns_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, digrev, cols, jobs);

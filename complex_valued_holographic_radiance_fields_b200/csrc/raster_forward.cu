@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(128) render_forward_kernel(
   __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
   __shared__ float4 s_c1[NB];      // (i10, i10, i11, i11)
   __shared__ float s_w[K][NB];
+  __shared__ int s_pm[NB];           // planes with weight >= 1e-6 (bit p)
   __shared__ float2 s_cp[C][NB];
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
@@ -171,8 +172,14 @@ __global__ void __launch_bounds__(128) render_forward_kernel(
         s_o[threadIdx.x] = make_float2(r0.z, r0.z);
         s_c0[threadIdx.x] = make_float4(cn.x, cn.x, cn.y, cn.y);
         s_c1[threadIdx.x] = make_float4(cn.z, cn.z, cn.w, cn.w);
+        int pm = 0;
 #pragma unroll
-        for (int p = 0; p < K; ++p) s_w[p][threadIdx.x] = plane_probs[gi * K + p];
+        for (int p = 0; p < K; ++p) {
+          const float w = plane_probs[gi * K + p];
+          s_w[p][threadIdx.x] = w;
+          pm |= (w >= kPlaneCutoff) ? (1 << p) : 0;
+        }
+        s_pm[threadIdx.x] = pm;
 #pragma unroll
         for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
       }
@@ -190,13 +197,15 @@ __global__ void __launch_bounds__(128) render_forward_kernel(
       const float2 power = __fmul2_rn(make_float2(-0.5f, -0.5f), __ffma2_rn(dx, u, __fmul2_rn(dy, v)));
       const bool ok0 = power.x <= 0.0f, ok1 = power.y <= 0.0f;
       if (!ok0 && !ok1) continue;
+      const int pm = s_pm[jj];
+      if (pm == 0) continue;
       const float2 og = __fmul2_rn(s_o[jj], make_float2(expf(power.x), expf(power.y)));
       const int pos = base + jj + 1;
-      bool all = true;
+      bool flip = false;
 #pragma unroll
       for (int p = 0; p < K; ++p) {
-        const float w = s_w[p][jj];
-        if (w >= kPlaneCutoff) {
+        if (pm & (1 << p)) {
+          const float w = s_w[p][jj];
           const bool a0 = ok0 && !done0[p], a1 = ok1 && !done1[p];
           if (a0 || a1) {
             const float2 aw = __fmul2_rn(og, make_float2(w, w));
@@ -211,13 +220,17 @@ __global__ void __launch_bounds__(128) render_forward_kernel(
               acc0[p][c] = __ffma2_rn(wt0, col, acc0[p][c]);
               acc1[p][c] = __ffma2_rn(wt1, col, acc1[p][c]);
             }
-            if (a0) { T[p].x = test.x; last0[p] = pos; done0[p] = test.x < 0.0001f; }
-            if (a1) { T[p].y = test.y; last1[p] = pos; done1[p] = test.y < 0.0001f; }
+            if (a0) { T[p].x = test.x; last0[p] = pos; if (test.x < 0.0001f) { done0[p] = true; flip = true; } }
+            if (a1) { T[p].y = test.y; last1[p] = pos; if (test.y < 0.0001f) { done1[p] = true; flip = true; } }
           }
         }
-        all = all && done0[p] && done1[p];
       }
-      alldone = all;
+      if (flip) {
+        bool all = true;
+#pragma unroll
+        for (int p = 0; p < K; ++p) all = all && done0[p] && done1[p];
+        alldone = all;
+      }
     }
   }
   const size_t HW = (size_t)H * W, pix = (size_t)py * W + px;

@@ -21,6 +21,8 @@ from . import _lib
 from .profiling import timed
 
 _F32 = torch.float32
+# (tile, Gaussian) pair count of the most recent forward (diagnostics / benchmarking)
+last_num_pairs = 0
 
 
 def _p(t):
@@ -77,6 +79,8 @@ def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_s
         _lib.check(L.cvhrf_raster_forward_geometry(ctypes.byref(sc), _p(geom), gbytes, _p(counts), st),
                    "cvhrf_raster_forward_geometry")
     num_pairs, num_visible = (int(v) for v in counts.cpu().tolist())  # one host sync (the reference has four)
+    global last_num_pairs
+    last_num_pairs = num_pairs
     bbytes = L.cvhrf_raster_binning_workspace_bytes(N, num_pairs, W, H)
     binws = torch.empty(bbytes, dtype=torch.uint8, device=dev)
     T = ((W + 15) // 16) * ((H + 15) // 16)

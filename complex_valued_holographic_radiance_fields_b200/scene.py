@@ -38,6 +38,17 @@ class PinholeCamera:
         if self.T is None:
             self.T = torch.tensor([0.0, 0.0, 4.0])
 
+    def on(self, device):
+        """(R, T) as contiguous float32 tensors on `device`, copied once and cached (a
+        per-step host-to-device copy from pageable memory would synchronise the GPU)."""
+        dev = torch.device(device)
+        cache = self.__dict__.setdefault("_dev_cache", {})
+        key = (str(dev), self.R.data_ptr(), self.T.data_ptr())
+        if key not in cache:
+            cache.clear()
+            cache[key] = (self.R.to(dev, torch.float32).contiguous(), self.T.to(dev, torch.float32).contiguous())
+        return cache[key]
+
     @property
     def fx(self):
         return (self.W / 2.0) / math.tan(self.fov / 2.0)
@@ -127,8 +138,7 @@ def render_inputs(params, camera):
     depth-sorted subset back to rows of `params`.
     """
     dev = params["means"].device
-    R = camera.R.to(dev)
-    T = camera.T.to(dev)
+    R, T = camera.on(dev)
     cam_all = params["means"] @ R + T
     z_all = cam_all[:, 2]
     valid = torch.where((z_all > camera.near) & (z_all < camera.far))[0]
@@ -210,10 +220,11 @@ class FusedRenderInputs(torch.autograd.Function):
 
 def render_inputs_fused(params, camera):
     """Same contract as `render_inputs`, through the fused kernels (all rows, culled by depth)."""
-    outs = FusedRenderInputs.apply(*[params[k] for k in _PARAM_ORDER], camera.R, camera.T, camera.near, camera.far)
+    R, T = camera.on(params["means"].device)
+    outs = FusedRenderInputs.apply(*[params[k] for k in _PARAM_ORDER], R, T, camera.near, camera.far)
     cam, z, q, s, col, ph, op, pl, order = outs
     kw = dict(cam_means_3D=cam, z_vals=z, quats=q, scales=s, colours=col, phase=ph, opacities=op, plane_probs=pl,
               fx=camera.fx, fy=camera.fy, px=camera.px, py=camera.py,
-              view_matrix=camera.R.to(params["means"].device, torch.float32).contiguous(),
+              view_matrix=R,
               img_size=(camera.W, camera.H), near_plane=camera.near, far_plane=camera.far)
     return kw, order.long()
