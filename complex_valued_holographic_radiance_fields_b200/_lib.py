@@ -8,7 +8,7 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcvhrf.so")
+LIB_PATH = os.environ.get("CVHRF_LIB") or os.path.join(_HERE, "libcvhrf.so")
 _lock = threading.Lock()
 _lib = None
 

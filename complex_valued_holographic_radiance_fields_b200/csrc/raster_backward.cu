@@ -129,7 +129,7 @@ __device__ __forceinline__ void bwd_pixel(PixState<C>& st, const BwdG& g, float 
 // for each of those reduces the per-pixel contributions over the CTA into the pair's
 // record (records start at zero; each pass adds its plane's share).
 template <int C>
-__global__ void __launch_bounds__(128, 4) render_backward_kernel(
+__global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
     const float4* __restrict__ rec0, const float4* __restrict__ cov2d, const float* __restrict__ colours,
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,

@@ -290,7 +290,11 @@ extern "C" int cvhrf_raster_forward_geometry(const cvhrf_raster_scene* scene, vo
     preprocess_kernel<<<nb, 256, 0, st>>>(s, cam, g);
     CVHRF_LAUNCH_CHECK();
     int alt = 0, rc;
-    if ((rc = radix_sort_pairs(g.key, g.order, g.key_alt, g.order_alt, N, 0, 32, g.scratch, st, &alt))) return rc;
+    // callers usually pass Gaussians already in depth order (Scene.render sorts them):
+    // then the 4 sort passes are skipped on the device
+    if ((rc = keys_sorted_flag(g.key, N, g.sorted, st))) return rc;
+    if ((rc = radix_sort_pairs(g.key, g.order, g.key_alt, g.order_alt, N, 0, 32, g.scratch, st, &alt, g.sorted)))
+      return rc;
     if (alt) {  // 4 passes of 8 bits always end in the primary buffers; kept for safety
       CVHRF_CUDA_TRY(cudaMemcpyAsync(g.order, g.order_alt, N * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
     }

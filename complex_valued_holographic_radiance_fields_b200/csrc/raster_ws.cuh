@@ -24,6 +24,7 @@ struct GeomWs {
   uint32_t* offsets;   // N   inclusive scan of tiles in depth order
   uint32_t* vis;       // N   visibility flag, then its inclusive scan
   uint32_t* scratch;   // scan / sort scratch
+  int* sorted;         // 1: depth keys already in order (the depth sort is skipped)
   size_t bytes;
 };
 
@@ -45,6 +46,7 @@ inline GeomWs carve_geom(void* base, size_t cap, int N, int C) {
   g.vis = cv.take<uint32_t>(N);
   const size_t sw = sort_scratch_words(N) > scan_scratch_words(N) ? sort_scratch_words(N) : scan_scratch_words(N);
   g.scratch = cv.take<uint32_t>(sw);
+  g.sorted = cv.take<int>(1);
   g.bytes = cv.overflow ? 0 : cv.used;
   return g;
 }

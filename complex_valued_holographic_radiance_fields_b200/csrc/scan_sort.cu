@@ -102,7 +102,9 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t
 
 // ---- radix sort -----------------------------------------------------------------
 __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint32_t* __restrict__ keys, int n, int shift,
-                                                                  int radix, uint32_t* __restrict__ hist, int nb) {
+                                                                  int radix, uint32_t* __restrict__ hist, int nb,
+                                                                  const int* __restrict__ skip) {
+  if (skip && *skip) return;
   __shared__ uint32_t h[256];
   for (int d = threadIdx.x; d < 256; d += blockDim.x) h[d] = 0;
   __syncthreads();
@@ -120,7 +122,9 @@ __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint32_t
 // Stable scatter: items are ranked in their original order (round, warp, lane).
 __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
     const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin, uint32_t* __restrict__ kout,
-    uint32_t* __restrict__ vout, int n, int shift, int radix, const uint32_t* __restrict__ incl, int nb) {
+    uint32_t* __restrict__ vout, int n, int shift, int radix, const uint32_t* __restrict__ incl, int nb,
+    const int* __restrict__ skip) {
+  if (skip && *skip) return;
   constexpr int NW = kSortThreads / 32;
   __shared__ uint32_t offs[256];
   __shared__ uint32_t wc[NW][256];
@@ -173,6 +177,21 @@ __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
 
 }  // namespace
 
+__global__ void flag_set_kernel(int* flag) { *flag = 1; }
+
+__global__ void sorted_check_kernel(const uint32_t* __restrict__ keys, int n, int* flag) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i + 1 < n && keys[i] > keys[i + 1]) *flag = 0;
+}
+
+int keys_sorted_flag(const uint32_t* keys, int n, int* flag, cudaStream_t st) {
+  flag_set_kernel<<<1, 1, 0, st>>>(flag);
+  sorted_check_kernel<<<(n + 255) / 256, 256, 0, st>>>(keys, n, flag);
+  count_launch(1);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
 size_t scan_scratch_words(int n) { return (size_t)scan_blocks(n) + 64; }
 
 int inclusive_scan_u32(const uint32_t* in, uint32_t* out, int n, uint32_t* scratch, cudaStream_t st) {
@@ -192,7 +211,7 @@ size_t sort_scratch_words(int n) {
 }
 
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
-                     uint32_t* scratch, cudaStream_t st, int* result_in_alt) {
+                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip) {
   *result_in_alt = 0;
   if (n <= 1 || end_bit <= begin_bit) return CVHRF_OK;
   const int nb = sort_blocks(n);
@@ -203,11 +222,11 @@ int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int
   for (int b = begin_bit; b < end_bit; b += kSortBits) {
     const int bits = min(kSortBits, end_bit - b);
     const int radix = 1 << bits;
-    radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, n, b, radix, hist, nb);
+    radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, n, b, radix, hist, nb, skip);
     count_launch(1);
     int rc = inclusive_scan_u32(hist, hist, radix * nb, sscr, st);
     if (rc) return rc;
-    radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, ko, vo, n, b, radix, hist, nb);
+    radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, ko, vo, n, b, radix, hist, nb, skip);
     CVHRF_LAUNCH_CHECK();
     uint32_t* t;
     t = ki; ki = ko; ko = t;

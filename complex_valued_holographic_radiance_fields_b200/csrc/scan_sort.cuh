@@ -29,8 +29,13 @@ int inclusive_scan_u32(const uint32_t* in, uint32_t* out, int n, uint32_t* scrat
 // Scratch (u32 count) for sorting n pairs.
 size_t sort_scratch_words(int n);
 // Stable sort by key bits [begin_bit, end_bit).  Ping-pongs between (k0,v0) and (k1,v1);
-// sets *result_in_alt to 1 if the sorted result ended in (k1, v1).
+// sets *result_in_alt to 1 if the sorted result ended in (k1, v1).  If `skip` (device int)
+// is non-null and non-zero when the passes run, every pass is a no-op: with an even
+// number of passes the (already sorted) input stays in (k0, v0), which is what a stable
+// sort of sorted keys with values 0..n-1 produces.
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
-                     uint32_t* scratch, cudaStream_t st, int* result_in_alt);
+                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip = nullptr);
+// *flag = 1 if keys[0..n) is non-decreasing, else 0 (device int, stream-ordered).
+int keys_sorted_flag(const uint32_t* keys, int n, int* flag, cudaStream_t st);
 
 }  // namespace cvhrf
