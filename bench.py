@@ -157,8 +157,10 @@ def run_mine(args, world, rank, local):
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
+        h0 = time.perf_counter()
         for _ in range(args.steps):
             loss = step()
+        host_ms = (time.perf_counter() - h0) * 1e3 / args.steps
         t1.record()
         barrier()
     sampler.__exit__()
@@ -220,6 +222,7 @@ def run_mine(args, world, rank, local):
         "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "iters/s",
                 "h2d_bytes_per_step": host_tgt.numel() * 4, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
+        "host_issue_ms_per_step": round(host_ms, 4),
         "ops_ms": {k: round(v[1], 4) for k, v in opsum.items()},
         "dominant_op": dom[0],
         "roofline": roof,

@@ -46,6 +46,8 @@ SIGNATURES = {
                             + [c_void_p] * 9 + [c_void_p]),
     "cvhrf_scene_backward": (c_int, [c_void_p, c_void_p, c_void_p] + [c_void_p] * 14 + [c_void_p]),
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
+    "cvhrf_sparse_adam_masked": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
+    "cvhrf_rows_to_mask": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
 }
 
 

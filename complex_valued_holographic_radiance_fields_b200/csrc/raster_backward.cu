@@ -295,21 +295,41 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   }
 }
 
-__global__ void __launch_bounds__(128) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
-                                                            const float* __restrict__ records, float* gcam,
-                                                            float* gz, float* gq, float* gs, float* gcol,
-                                                            float* gph, float* gop, float* gpl) {
-  const int si = blockIdx.x * blockDim.x + threadIdx.x;
-  if (si >= s.N) return;
+// One CTA per 128 consecutive Gaussians (depth order).  Phase 1 sums each Gaussian's
+// contiguous records with coalesced loads (a half-warp per Gaussian when a record has
+// <= 16 floats, a warp otherwise; lane = record component).  Phase 2: one thread per
+// Gaussian chains the sums through the projection.
+constexpr int kGradBlock = 128;
+constexpr int kRecMax = 6 + kMaxPlanes + 2 * kMaxChannels;
+
+__global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
+                                                                   const float* __restrict__ records, float* gcam,
+                                                                   float* gz, float* gq, float* gs, float* gcol,
+                                                                   float* gph, float* gop, float* gpl) {
+  __shared__ float s_r[kGradBlock][kRecMax + 1];
   const int K = s.K, C = s.C, VR = 6 + K + 2 * C;
+  const int s0 = blockIdx.x * kGradBlock;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int width = VR <= 16 ? 16 : 32;            // lanes per Gaussian
+  const int per_warp = 32 / width;
+  const int sub = lane / width, comp = lane - sub * width;
+  for (int lg = warp * per_warp + sub; lg < kGradBlock; lg += (kGradBlock / 32) * per_warp) {
+    const int si = s0 + lg;
+    float acc = 0.f;
+    if (si < s.N && comp < VR) {
+      const uint32_t a = si == 0 ? 0u : g.offsets[si - 1], b = g.offsets[si];
+      const float* rec = records + (size_t)a * VR + comp;
+#pragma unroll 4
+      for (uint32_t k = a; k < b; ++k, rec += VR) acc += *rec;
+    }
+    if (comp < VR) s_r[lg][comp] = acc;
+  }
+  __syncthreads();
+  const int si = s0 + threadIdx.x;
+  if (si >= s.N) return;
+  const float* r = s_r[threadIdx.x];
   const uint32_t gi = g.order[si];
   const uint32_t a = si == 0 ? 0u : g.offsets[si - 1], b = g.offsets[si];
-  float r[6 + kMaxPlanes + 2 * kMaxChannels];
-  for (int i = 0; i < VR; ++i) r[i] = 0.f;
-  for (uint32_t k = a; k < b; ++k) {
-    const float* rec = records + (size_t)k * VR;
-    for (int i = 0; i < VR; ++i) r[i] += rec[i];
-  }
   float dcam[3] = {0.f, 0.f, 0.f}, dq[4] = {0.f, 0.f, 0.f, 0.f}, ds[3] = {0.f, 0.f, 0.f};
   if (b > a) {
     float Wm[9];
@@ -381,7 +401,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
 #undef CVHRF_BWD
     CVHRF_LAUNCH_CHECK();
   }
-  gaussian_grad_kernel<<<(s.N + 127) / 128, 128, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
+  gaussian_grad_kernel<<<(s.N + kGradBlock - 1) / kGradBlock, kGradBlock, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
                                                           grad_scales, grad_colours, grad_phase, grad_opacities,
                                                           grad_plane_probs);
   CVHRF_LAUNCH_CHECK();

@@ -72,3 +72,72 @@ extern "C" int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, co
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
+
+// ---- row-mask form: every row streamed in order, updated where mask[row] != 0 ----
+// Same update as cvhrf_sparse_adam; rows are visited in memory order (coalesced) instead
+// of through the visible-index gather, which is faster when most rows are visible and
+// lets a visibility union (e.g. an all-reduce MAX over ranks) be used without compaction.
+namespace cvhrf {
+namespace {
+
+__global__ void __launch_bounds__(256) sparse_adam_masked_kernel(AdamLaunch L, const uint8_t* __restrict__ mask,
+                                                                 int mask_len, float b1, float b2) {
+  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= L.start[L.n]) return;
+  int gi = 0;
+#pragma unroll 1
+  while (gi + 1 < L.n && e >= L.start[gi + 1]) ++gi;
+  const cvhrf_adam_group& G = L.g[gi];
+  const long long local = e - L.start[gi];
+  const long long row = local / G.D;
+  if (!G.dense && (row >= mask_len || mask[row] == 0)) return;
+  const size_t idx = (size_t)local;
+  const float Register_param_grad = G.grad[idx];
+  float Register_exp_avg = G.exp_avg[idx];
+  float Register_exp_avg_sq = G.exp_avg_sq[idx];
+  Register_exp_avg = b1 * Register_exp_avg + (1.0f - b1) * Register_param_grad;
+  Register_exp_avg_sq = b2 * Register_exp_avg_sq + (1.0f - b2) * Register_param_grad * Register_param_grad;
+  const float step = -G.lr * Register_exp_avg / (sqrtf(Register_exp_avg_sq) + G.eps);
+  G.param[idx] += step;
+  G.exp_avg[idx] = Register_exp_avg;
+  G.exp_avg_sq[idx] = Register_exp_avg_sq;
+}
+
+__global__ void rows_to_mask_kernel(const int64_t* __restrict__ rows, int V, int mask_len, uint8_t* mask) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < V && rows[i] >= 0 && rows[i] < mask_len) mask[rows[i]] = 1;
+}
+
+}  // namespace
+}  // namespace cvhrf
+
+extern "C" int cvhrf_rows_to_mask(const int64_t* rows, int V, uint8_t* mask, int mask_len, void* stream) {
+  if (V < 0 || mask_len < 0 || (V > 0 && !rows) || (mask_len > 0 && !mask)) return CVHRF_EINVAL;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (mask_len > 0) CVHRF_CUDA_TRY(cudaMemsetAsync(mask, 0, (size_t)mask_len, st));
+  if (V == 0) return CVHRF_OK;
+  rows_to_mask_kernel<<<(V + 255) / 256, 256, 0, st>>>(rows, V, mask_len, mask);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+extern "C" int cvhrf_sparse_adam_masked(const cvhrf_adam_group* groups, int ngroups, const uint8_t* mask,
+                                        int mask_len, float b1, float b2, void* stream) {
+  if (!groups || ngroups < 0 || ngroups > kMaxGroups || mask_len < 0 || (mask_len > 0 && !mask)) return CVHRF_EINVAL;
+  AdamLaunch L{};
+  long long tot = 0;
+  for (int i = 0; i < ngroups; ++i) {
+    const cvhrf_adam_group& g = groups[i];
+    if (g.D < 1 || g.N < 0 || !g.param || !g.grad || !g.exp_avg || !g.exp_avg_sq) return CVHRF_EINVAL;
+    if (g.N == 0) continue;
+    L.g[L.n] = g;
+    L.start[L.n] = tot;
+    tot += (long long)g.N * g.D;
+    ++L.n;
+  }
+  L.start[L.n] = tot;
+  if (tot == 0) return CVHRF_OK;
+  sparse_adam_masked_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, (cudaStream_t)stream>>>(L, mask, mask_len, b1, b2);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}

@@ -32,13 +32,47 @@ def allreduce_gradients_and_visibility(params, visible_rows, n_rows, group=None)
     return torch.nonzero(mask, as_tuple=False).squeeze(1)
 
 
+def _shared_flat_buffer(params):
+    """The flat buffer all .grad tensors are views of (FusedRenderInputs backward), or None."""
+    from .scene import FusedRenderInputs
+    flat = getattr(FusedRenderInputs, "last_grad_buffer", None)
+    if flat is None:
+        return None
+    base = flat.untyped_storage().data_ptr()
+    total = 0
+    for p in params.values():
+        if p.grad is None or p.grad.untyped_storage().data_ptr() != base:
+            return None
+        total += p.grad.numel()
+    return flat if total == flat.numel() else None
+
+
 def dp_step(trainer, target=None, group=None):
-    """One view-parallel training iteration on `trainer` (a HoloTrainer)."""
+    """One view-parallel training iteration on `trainer` (a HoloTrainer).
+
+    The gradients are summed with one in-place all-reduce of the flat buffer they share
+    and the visible rows with one all-reduce (MAX) of a row mask that goes straight to
+    the masked sparse Adam, so the exchange needs no copy and no host synchronisation.
+    """
+    from . import _lib
+    import ctypes
     for p in trainer.params.values():
         p.grad = None
     loss, visible = trainer.forward(target)
     loss.backward()
     n = trainer.params["means"].shape[0]
-    visible = allreduce_gradients_and_visibility(trainer.params, visible, n, group)
-    trainer.opt.step(visible)
+    flat = _shared_flat_buffer(trainer.params)
+    if flat is None:  # gradients not in one buffer: fall back to the concatenating exchange
+        visible = allreduce_gradients_and_visibility(trainer.params, visible, n, group)
+        trainer.opt.step(visible)
+        return loss.detach()
+    mask = torch.empty(n, dtype=torch.uint8, device=flat.device)
+    vis = visible.to(torch.int64).contiguous()
+    _lib.check(_lib.lib().cvhrf_rows_to_mask(ctypes.c_void_p(vis.data_ptr()), vis.numel(),
+                                             ctypes.c_void_p(mask.data_ptr()), n,
+                                             ctypes.c_void_p(torch.cuda.current_stream(flat.device).cuda_stream)),
+               "cvhrf_rows_to_mask")
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=group)
+    trainer.opt.step(row_mask=mask)
     return loss.detach()

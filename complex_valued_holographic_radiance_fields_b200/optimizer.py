@@ -44,9 +44,16 @@ class SparseGaussianAdam(torch.optim.Adam):
         super().__init__(params=params, lr=lr, eps=eps)
 
     @torch.no_grad()
-    def step(self, visible_chunk):
+    def step(self, visible_chunk=None, row_mask=None):
+        """Update the rows listed in `visible_chunk` (int64 row indices, as the reference)
+        or, alternatively, the rows where `row_mask` (uint8/bool, one entry per row) is set.
+        1-D parameters are updated densely.  With indices and none visible nothing is
+        updated (optimizer.py:197-199); a mask is used as given (no host synchronisation)."""
         groups, keep = [], []
-        vis = visible_chunk.to(torch.int64).contiguous()
+        if row_mask is None:
+            vis = visible_chunk.to(torch.int64).contiguous()
+            if vis.numel() == 0:
+                vis = None
         device = None
         for group in self.param_groups:
             assert len(group["params"]) == 1, "more than one tensor in group"
@@ -58,7 +65,7 @@ class SparseGaussianAdam(torch.optim.Adam):
                 state["step"] = torch.tensor(0.0, dtype=torch.float32)
                 state["exp_avg"] = torch.zeros_like(param, memory_format=torch.preserve_format)
                 state["exp_avg_sq"] = torch.zeros_like(param, memory_format=torch.preserve_format)
-            if vis.numel() == 0:
+            if row_mask is None and vis is None:
                 continue
             if not (param.is_cuda and param.dtype == torch.float32 and param.is_contiguous()):
                 raise RuntimeError("SparseGaussianAdam needs contiguous float32 CUDA parameters")
@@ -80,8 +87,26 @@ class SparseGaussianAdam(torch.optim.Adam):
             device = param.device
         if groups:
             with timed("sparse_adam"):
+                n_rows = max(g.N for g in groups)
+                L = _lib.lib()
+                st = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+                if row_mask is None:
+                    mask = self._mask_buffer(n_rows, device)
+                    _lib.check(L.cvhrf_rows_to_mask(ctypes.c_void_p(vis.data_ptr()), vis.numel(),
+                                                    ctypes.c_void_p(mask.data_ptr()), n_rows, st),
+                               "cvhrf_rows_to_mask")
+                else:
+                    mask = row_mask.to(torch.uint8).contiguous()
                 for i in range(0, len(groups), 16):
-                    _launch(groups[i:i + 16], vis, 0.9, 0.999, device)
+                    arr = (_lib.AdamGroup * len(groups[i:i + 16]))(*groups[i:i + 16])
+                    _lib.check(L.cvhrf_sparse_adam_masked(arr, len(groups[i:i + 16]), ctypes.c_void_p(mask.data_ptr()),
+                                                          mask.numel(), 0.9, 0.999, st), "cvhrf_sparse_adam_masked")
+
+    def _mask_buffer(self, n, device):
+        buf = getattr(self, "_row_mask_buf", None)
+        if buf is None or buf.numel() < n or buf.device != device:
+            buf = self._row_mask_buf = torch.empty(n, dtype=torch.uint8, device=device)
+        return buf[:n]
 
 
 def sparse_adam_update(param, grad, exp_avg, exp_avg_sq, visible_chunk, lr, b1, b2, eps):

@@ -210,7 +210,14 @@ class FusedRenderInputs(torch.autograd.Function):
             return torch.zeros(shape, dtype=torch.float32, device=dev) if t is None else t.contiguous()
         gs = [g(g_cam, (N, 3)), g(g_q, (N, 4)), g(g_s, (N, 3)), g(g_col, (N, C)), g(g_ph, (N, C)), g(g_op, (N,)),
               g(g_pl, (N, K))]
-        d = [torch.empty_like(t) for t in ins]
+        # all parameter gradients live in ONE flat buffer (views), so a data-parallel
+        # exchange can all-reduce them in place without a concatenating copy
+        flat = torch.empty(sum(t.numel() for t in ins), dtype=torch.float32, device=dev)
+        d, off = [], 0
+        for t in ins:
+            d.append(flat[off:off + t.numel()].view_as(t))
+            off += t.numel()
+        FusedRenderInputs.last_grad_buffer = flat
         st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
         _lib.check(_lib.lib().cvhrf_scene_backward(ctypes.byref(G), R.data_ptr(), order.data_ptr(),
                                                      *[t.data_ptr() for t in gs], *[t.data_ptr() for t in d], st),

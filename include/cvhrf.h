@@ -213,6 +213,14 @@ typedef struct {
  */
 int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, const int64_t* visible, int V,
                       float beta1, float beta2, void* stream);
+/*
+ * The same update with the visible rows given as a row mask (uint8, mask_len rows,
+ * non-zero = update; dense groups ignore it).  Rows are streamed in memory order.
+ * cvhrf_rows_to_mask builds such a mask from row indices (zeroes it first).
+ */
+int cvhrf_sparse_adam_masked(const cvhrf_adam_group* groups, int ngroups, const uint8_t* mask, int mask_len,
+                             float beta1, float beta2, void* stream);
+int cvhrf_rows_to_mask(const int64_t* rows, int V, uint8_t* mask, int mask_len, void* stream);
 
 /* ---- caller glue: filter, depth sort, gather, activations ---------------------- */
 /*
