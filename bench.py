@@ -18,6 +18,7 @@ pure-torch propagation on torch CPU) on rank 0, and, beside it, the reference's 
 CUDA kernels rebuilt for sm_100a on this GPU (field `reference_cuda_sm100a`).
 """
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -137,23 +138,34 @@ def run_mine(args, world, rank, local):
     torch.cuda.set_device(dev)
     cam = SC.look_at_camera(IMG, IMG, 2 * math.pi * rank / max(world, 1), 0.0) if world > 1 else None
     tr = HoloTrainer(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES, device=dev, camera=cam)
-    step = (lambda t=None: dp_step(tr, t)) if world > 1 else (lambda t=None: tr.step(t))
-    sampler = ClockSampler(local)   # sampling starts with the warm-up so the loaded period is covered
-    sampler.__enter__()
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    L = _lib.lib()
 
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
+    graph = os.environ.get("CVHRF_BENCH_EAGER", "0") != "1"
+    sampler = ClockSampler(local)   # sampling starts with the warm-up so the loaded period is covered
+    sampler.__enter__()
+    L = _lib.lib()
+    if graph:
+        # one CUDA graph per iteration (forward, backward, exchange, optimizer); capture()
+        # runs eager warm-up iterations itself, then W replays warm the graph
+        from complex_valued_holographic_radiance_fields_b200.distributed import graph_exchange
+        ex = graph_exchange() if world > 1 else None
+        tr.capture(headroom=1.5, exchange=ex, warmup=2,
+                   eager_step=(lambda: dp_step(tr)) if world > 1 else None)
+        step = tr.replay
+    else:
+        step = (lambda t=None: dp_step(tr, t)) if world > 1 else (lambda t=None: tr.step(t))
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
     # --- device-timed region: inputs resident in HBM ---
     barrier()
     launches0 = L.cvhrf_kernel_launch_count()
-    with op_timing() as ops:
+    with contextlib.nullcontext() if graph else op_timing() as ops:
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -165,6 +177,15 @@ def run_mine(args, world, rank, local):
         barrier()
     sampler.__exit__()
     launches = L.cvhrf_kernel_launch_count() - launches0
+    if graph:
+        launches = tr.graph_launches * args.steps   # replays launch the captured kernels
+        if tr.graph_overflowed():
+            raise RuntimeError("pair capacity exceeded during the timed replays; raise the headroom")
+        # per-operator device times (roofline) from a few eager iterations, outside the timed region
+        with op_timing() as ops:
+            for _ in range(3):
+                (dp_step(tr) if world > 1 else tr.step())
+        barrier()
     ms = t0.elapsed_time(t1) / args.steps
     opsum = ops.summary()
     ms_t = torch.tensor([ms], device=dev)
@@ -180,8 +201,11 @@ def run_mine(args, world, rank, local):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        dev_tgt.copy_(host_tgt, non_blocking=True)
-        float(step(dev_tgt).item())
+        if graph:
+            float(tr.replay(host_tgt).item())     # pinned host target -> static device buffer inside
+        else:
+            dev_tgt.copy_(host_tgt, non_blocking=True)
+            float(step(dev_tgt).item())
     e1.record()
     barrier()
     e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
@@ -223,6 +247,8 @@ def run_mine(args, world, rank, local):
                 "h2d_bytes_per_step": host_tgt.numel() * 4, "d2h_bytes_per_step": 4},
         "gpu_launches": int(launches),
         "host_issue_ms_per_step": round(host_ms, 4),
+        "execution": "cuda_graph (one replay per iteration; pair capacity %d)" % tr.pairs_capacity if graph
+                     else "eager",
         "ops_ms": {k: round(v[1], 4) for k, v in opsum.items()},
         "dominant_op": dom[0],
         "roofline": roof,

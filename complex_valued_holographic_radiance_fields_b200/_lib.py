@@ -38,6 +38,8 @@ SIGNATURES = {
     "cvhrf_raster_binning_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "cvhrf_raster_forward_render": (c_int, [c_void_p, c_void_p, c_size_t, c_int, c_int, c_void_p, c_size_t,
                                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "cvhrf_raster_forward_render_capacity": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_int, c_void_p,
+                                                     c_size_t] + [c_void_p] * 8),
     "cvhrf_raster_backward_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cvhrf_raster_backward": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_size_t, c_int, c_void_p, c_void_p,
                                       c_void_p, c_void_p, c_void_p, c_void_p, c_size_t] + [c_void_p] * 9),

@@ -305,7 +305,8 @@ constexpr int kRecMax = 6 + kMaxPlanes + 2 * kMaxChannels;
 __global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
                                                                    const float* __restrict__ records, float* gcam,
                                                                    float* gz, float* gq, float* gs, float* gcol,
-                                                                   float* gph, float* gop, float* gpl) {
+                                                                   float* gph, float* gop, float* gpl,
+                                                                   uint32_t max_slot) {
   __shared__ float s_r[kGradBlock][kRecMax + 1];
   const int K = s.K, C = s.C, VR = 6 + K + 2 * C;
   const int s0 = blockIdx.x * kGradBlock;
@@ -317,7 +318,8 @@ __global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_
     const int si = s0 + lg;
     float acc = 0.f;
     if (si < s.N && comp < VR) {
-      const uint32_t a = si == 0 ? 0u : g.offsets[si - 1], b = g.offsets[si];
+      // records exist for slots < max_slot (the pair capacity in capacity mode)
+      const uint32_t a = min(si == 0 ? 0u : g.offsets[si - 1], max_slot), b = min(g.offsets[si], max_slot);
       const float* rec = records + (size_t)a * VR + comp;
 #pragma unroll 4
       for (uint32_t k = a; k < b; ++k, rec += VR) acc += *rec;
@@ -329,7 +331,7 @@ __global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_
   if (si >= s.N) return;
   const float* r = s_r[threadIdx.x];
   const uint32_t gi = g.order[si];
-  const uint32_t a = si == 0 ? 0u : g.offsets[si - 1], b = g.offsets[si];
+  const uint32_t a = min(si == 0 ? 0u : g.offsets[si - 1], max_slot), b = min(g.offsets[si], max_slot);
   float dcam[3] = {0.f, 0.f, 0.f}, dq[4] = {0.f, 0.f, 0.f, 0.f}, ds[3] = {0.f, 0.f, 0.f};
   if (b > a) {
     float Wm[9];
@@ -403,7 +405,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
   }
   gaussian_grad_kernel<<<(s.N + kGradBlock - 1) / kGradBlock, kGradBlock, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
                                                           grad_scales, grad_colours, grad_phase, grad_opacities,
-                                                          grad_plane_probs);
+                                                          grad_plane_probs, (uint32_t)num_pairs);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }

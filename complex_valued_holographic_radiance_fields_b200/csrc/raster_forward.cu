@@ -72,13 +72,18 @@ __global__ void counts_kernel(const uint32_t* offsets, const uint32_t* vis_scan,
   counts[1] = N > 0 ? (int32_t)vis_scan[N - 1] : 0;
 }
 
-__global__ void __launch_bounds__(256) emit_pairs_kernel(GeomWs g, Camera cam, int N, BinWs b) {
+__global__ void __launch_bounds__(256) emit_pairs_kernel(GeomWs g, Camera cam, int N, BinWs b, uint32_t cap,
+                                                         int32_t* overflow) {
   const int si = blockIdx.x * blockDim.x + threadIdx.x;
   if (si >= N) return;
   const uint32_t gi = g.order[si];
   const uint32_t n = g.tiles[gi];
   if (n == 0) return;
   uint32_t slot = si == 0 ? 0u : g.offsets[si - 1];
+  if (slot + n > cap) {  // more pairs than the caller's capacity: flag it, emit nothing
+    if (overflow) *overflow = 1;
+    return;
+  }
   uint2 rmin, rmax;
   tile_rect(g.means2d[gi], g.radii[gi], cam.grid_x, cam.grid_y, rmin, rmax);
   for (uint32_t ty = rmin.y; ty < rmax.y; ++ty)
@@ -96,13 +101,30 @@ __global__ void clear_ranges_kernel(int2* ranges, int T) {
 }
 
 __global__ void ranges_kernel(const uint32_t* __restrict__ tkey, const uint32_t* __restrict__ slot,
-                              const uint32_t* __restrict__ gauss, int n, int2* ranges, int32_t* point_list) {
+                              const uint32_t* __restrict__ gauss, int n, int2* ranges, int32_t* point_list,
+                              const int32_t* __restrict__ n_dev) {
+  if (n_dev) n = min(n, *n_dev);
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const uint32_t t = tkey[i];
   point_list[i] = (int32_t)gauss[slot[i]];
   if (i == 0 || tkey[i - 1] != t) ranges[t].x = i;
   if (i == n - 1 || tkey[i + 1] != t) ranges[t].y = i + 1;
+}
+
+__global__ void capacity_count_kernel(const int32_t* counts, int cap, int32_t* eff, int32_t* overflow) {
+  const int n = counts[0];
+  const bool fits = n <= cap;
+  *eff = fits ? n : 0;
+  if (!fits) *overflow = 1;
+}
+
+__global__ void visible_mask_kernel(const float* __restrict__ cam_means, int N, float near_plane, float far_plane,
+                                    uint8_t* __restrict__ mask) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N) return;
+  const float zc = cam_means[3 * i + 2];
+  mask[i] = (zc > 0.2f && zc > near_plane && zc < far_plane) ? 1 : 0;
 }
 
 __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32_t* __restrict__ vis_scan, int N,
@@ -334,7 +356,7 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
   clear_ranges_kernel<<<(T + 255) / 256, 256, 0, st>>>((int2*)ranges, T);
   CVHRF_LAUNCH_CHECK();
   if (num_pairs > 0) {
-    emit_pairs_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(g, cam, s.N, b);
+    emit_pairs_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(g, cam, s.N, b, (uint32_t)num_pairs, nullptr);
     CVHRF_LAUNCH_CHECK();
     int alt = 0;
     if ((rc = radix_sort_pairs(b.tkey, b.slot, b.tkey_alt, b.slot_alt, num_pairs, 0, tile_bits(T), b.scratch, st,
@@ -345,12 +367,73 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
       CVHRF_CUDA_TRY(cudaMemcpyAsync(b.slot, b.slot_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
     }
     ranges_kernel<<<(num_pairs + 255) / 256, 256, 0, st>>>(b.tkey, b.slot, b.gauss, num_pairs, (int2*)ranges,
-                                                           point_list);
+                                                           point_list, nullptr);
     CVHRF_LAUNCH_CHECK();
   }
   if (num_visible > 0) {
     visible_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(s.cam_means, g.vis, s.N, s.near_plane, s.far_plane,
                                                       visible_indices);
+    CVHRF_LAUNCH_CHECK();
+  }
+  dim3 grid(T);
+  const int2* rg = (const int2*)ranges;
+  float2* f = (float2*)field;
+  switch (s.K) {
+    case 1: return launch_render_k<1>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 2: return launch_render_k<2>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 3: return launch_render_k<3>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 4: return launch_render_k<4>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 5: return launch_render_k<5>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 6: return launch_render_k<6>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    case 7: return launch_render_k<7>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+    default: return launch_render_k<8>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
+  }
+}
+
+// Same as cvhrf_raster_forward_render without the host round trip: the pair count stays in
+// counts_dev[0] (written by cvhrf_raster_forward_geometry), buffers are sized for
+// pairs_capacity, and *overflow is set when the count exceeds it (outputs then invalid).
+extern "C" int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* scene, const void* geom_ws,
+                                                    size_t geom_bytes, const int32_t* counts_dev, int pairs_capacity,
+                                                    void* bin_ws, size_t bin_bytes, void* field, float* final_Ts,
+                                                    int32_t* n_contrib, int32_t* point_list, int32_t* ranges,
+                                                    uint8_t* visible_mask, int32_t* overflow, void* stream) {
+  const int num_pairs = pairs_capacity;
+  if (!scene_ok(scene) || num_pairs < 1 || !counts_dev || !field || !final_Ts || !n_contrib || !ranges ||
+      !point_list || !overflow || (scene->N > 0 && !visible_mask))
+    return CVHRF_EINVAL;
+  const cvhrf_raster_scene& s = *scene;
+  bool ok;
+  GeomWs g = carve_geom_checked(const_cast<void*>(geom_ws), geom_bytes, s.N, s.C, ok);
+  if (!ok) return CVHRF_EWORKSPACE;
+  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs);
+  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  const Camera cam = make_camera(s);
+  const int T = cam.grid_x * cam.grid_y;
+  int rc;
+  clear_ranges_kernel<<<(T + 255) / 256, 256, 0, st>>>((int2*)ranges, T);
+  CVHRF_LAUNCH_CHECK();
+  capacity_count_kernel<<<1, 1, 0, st>>>(counts_dev, num_pairs, b.eff, overflow);
+  CVHRF_LAUNCH_CHECK();
+  if (num_pairs > 0) {
+    emit_pairs_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(g, cam, s.N, b, (uint32_t)num_pairs, overflow);
+    CVHRF_LAUNCH_CHECK();
+    int alt = 0;
+    if ((rc = radix_sort_pairs(b.tkey, b.slot, b.tkey_alt, b.slot_alt, num_pairs, 0, tile_bits(T), b.scratch, st,
+                               &alt, nullptr, b.eff)))
+      return rc;
+    if (alt) {  // keep the sorted result in the primary buffers (the backward reads b.slot)
+      CVHRF_CUDA_TRY(cudaMemcpyAsync(b.tkey, b.tkey_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+      CVHRF_CUDA_TRY(cudaMemcpyAsync(b.slot, b.slot_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
+    }
+    ranges_kernel<<<(num_pairs + 255) / 256, 256, 0, st>>>(b.tkey, b.slot, b.gauss, num_pairs, (int2*)ranges,
+                                                           point_list, b.eff);
+    CVHRF_LAUNCH_CHECK();
+  }
+  if (s.N > 0) {
+    visible_mask_kernel<<<(s.N + 255) / 256, 256, 0, st>>>(s.cam_means, s.N, s.near_plane, s.far_plane,
+                                                           visible_mask);
     CVHRF_LAUNCH_CHECK();
   }
   dim3 grid(T);

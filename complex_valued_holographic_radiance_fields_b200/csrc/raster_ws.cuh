@@ -59,6 +59,7 @@ struct BinWs {
   uint32_t* slot_alt;
   uint32_t* gauss;     // pairs: Gaussian index of each emission slot
   uint32_t* scratch;
+  int32_t* eff;        // capacity mode: pair count if it fits the capacity, else 0
   size_t bytes;
 };
 
@@ -72,6 +73,7 @@ inline BinWs carve_bin(void* base, size_t cap, int pairs) {
   b.slot_alt = cv.take<uint32_t>(n);
   b.gauss = cv.take<uint32_t>(n);
   b.scratch = cv.take<uint32_t>(sort_scratch_words(n));
+  b.eff = cv.take<int32_t>(1);
   b.bytes = cv.overflow ? 0 : cv.used;
   return b;
 }

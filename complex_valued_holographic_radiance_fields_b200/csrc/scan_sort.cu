@@ -103,8 +103,10 @@ __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t
 // ---- radix sort -----------------------------------------------------------------
 __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint32_t* __restrict__ keys, int n, int shift,
                                                                   int radix, uint32_t* __restrict__ hist, int nb,
-                                                                  const int* __restrict__ skip) {
+                                                                  const int* __restrict__ skip,
+                                                                  const int* __restrict__ n_dev) {
   if (skip && *skip) return;
+  if (n_dev) n = min(n, *n_dev);
   __shared__ uint32_t h[256];
   for (int d = threadIdx.x; d < 256; d += blockDim.x) h[d] = 0;
   __syncthreads();
@@ -123,8 +125,9 @@ __global__ void __launch_bounds__(kSortThreads) radix_hist_kernel(const uint32_t
 __global__ void __launch_bounds__(kSortThreads) radix_scatter_kernel(
     const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin, uint32_t* __restrict__ kout,
     uint32_t* __restrict__ vout, int n, int shift, int radix, const uint32_t* __restrict__ incl, int nb,
-    const int* __restrict__ skip) {
+    const int* __restrict__ skip, const int* __restrict__ n_dev) {
   if (skip && *skip) return;
+  if (n_dev) n = min(n, *n_dev);
   constexpr int NW = kSortThreads / 32;
   __shared__ uint32_t offs[256];
   __shared__ uint32_t wc[NW][256];
@@ -211,7 +214,7 @@ size_t sort_scratch_words(int n) {
 }
 
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
-                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip) {
+                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip, const int* n_dev) {
   *result_in_alt = 0;
   if (n <= 1 || end_bit <= begin_bit) return CVHRF_OK;
   const int nb = sort_blocks(n);
@@ -222,11 +225,11 @@ int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int
   for (int b = begin_bit; b < end_bit; b += kSortBits) {
     const int bits = min(kSortBits, end_bit - b);
     const int radix = 1 << bits;
-    radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, n, b, radix, hist, nb, skip);
+    radix_hist_kernel<<<nb, kSortThreads, 0, st>>>(ki, n, b, radix, hist, nb, skip, n_dev);
     count_launch(1);
     int rc = inclusive_scan_u32(hist, hist, radix * nb, sscr, st);
     if (rc) return rc;
-    radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, ko, vo, n, b, radix, hist, nb, skip);
+    radix_scatter_kernel<<<nb, kSortThreads, 0, st>>>(ki, vi, ko, vo, n, b, radix, hist, nb, skip, n_dev);
     CVHRF_LAUNCH_CHECK();
     uint32_t* t;
     t = ki; ki = ko; ko = t;

@@ -34,7 +34,10 @@ size_t sort_scratch_words(int n);
 // number of passes the (already sorted) input stays in (k0, v0), which is what a stable
 // sort of sorted keys with values 0..n-1 produces.
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
-                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip = nullptr);
+                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip = nullptr,
+                     const int* n_dev = nullptr);
+// (n_dev, when non-null, is a device count: only the first min(n, *n_dev) items are sorted;
+//  n is then the capacity the launch grids are sized for.)
 // *flag = 1 if keys[0..n) is non-decreasing, else 0 (device int, stream-ordered).
 int keys_sorted_flag(const uint32_t* keys, int n, int* flag, cudaStream_t st);
 

@@ -76,3 +76,16 @@ def dp_step(trainer, target=None, group=None):
     dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=group)
     trainer.opt.step(row_mask=mask)
     return loss.detach()
+
+
+def graph_exchange(group=None):
+    """The exchange of `dp_step` as a callback for `HoloTrainer.capture(exchange=...)`:
+    both all-reduces are recorded into the trainer's CUDA graph (NCCL supports capture)."""
+    def exchange(trainer, row_mask):
+        flat = _shared_flat_buffer(trainer.params)
+        if flat is None:
+            raise RuntimeError("graph capture needs the gradients in one flat buffer (render_inputs_fused)")
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+        dist.all_reduce(row_mask, op=dist.ReduceOp.MAX, group=group)
+        return row_mask
+    return exchange

@@ -56,8 +56,13 @@ def _stream(dev):
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_size, near, far):
-    """Run the forward; returns (field, info) where info holds everything the backward needs."""
+def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_size, near, far,
+                      pairs_capacity=None):
+    """Run the forward; returns (field, info) where info holds everything the backward needs.
+
+    With `pairs_capacity` the call makes no host round trip (CUDA-graph capturable): buffers
+    are sized for that many (tile, Gaussian) pairs, visibility comes back as a uint8 mask,
+    and info["overflow"] (device int32) becomes 1 if the scene needed more pairs."""
     dev = cam.device
     cam, z, q, s = (_prep(cam, "cam_means_3D"), _prep(z, "z_vals"), _prep(q, "quats"), _prep(s, "scales"))
     col, ph, op, pp = (_prep(col, "colours"), _prep(ph, "phase"), _prep(op, "opacities"), _prep(pp, "plane_probs"))
@@ -78,6 +83,9 @@ def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_s
     with timed("raster_geometry"):
         _lib.check(L.cvhrf_raster_forward_geometry(ctypes.byref(sc), _p(geom), gbytes, _p(counts), st),
                    "cvhrf_raster_forward_geometry")
+    if pairs_capacity is not None:
+        return _render_capacity(sc, geom, gbytes, counts, int(pairs_capacity), N, K, C, W, H, dev, st,
+                                (fx, fy, px, py, near, far))
     num_pairs, num_visible = (int(v) for v in counts.cpu().tolist())  # one host sync (the reference has four)
     global last_num_pairs
     last_num_pairs = num_pairs
@@ -97,6 +105,35 @@ def rasterize_forward(cam, z, q, s, col, ph, op, pp, fx, fy, px, py, view, img_s
     info = dict(geom=geom, gbytes=gbytes, binws=binws, bbytes=bbytes, num_pairs=num_pairs, final_Ts=final_Ts,
                 n_contrib=n_contrib, point_list=point_list, ranges=ranges, visible=vis, img=(W, H),
                 cam=(fx, fy, px, py, near, far))
+    return field, info
+
+
+last_counts = None
+
+
+def _render_capacity(sc, geom, gbytes, counts, cap, N, K, C, W, H, dev, st, camp):
+    global last_counts
+    L = _lib.lib()
+    cap = max(cap, 1)
+    bbytes = L.cvhrf_raster_binning_workspace_bytes(N, cap, W, H)
+    binws = torch.empty(bbytes, dtype=torch.uint8, device=dev)
+    T = ((W + 15) // 16) * ((H + 15) // 16)
+    field = torch.empty((K, C, H, W), dtype=torch.complex64, device=dev)
+    final_Ts = torch.empty((K, H, W), dtype=_F32, device=dev)
+    n_contrib = torch.empty((K, H, W), dtype=torch.int32, device=dev)
+    point_list = torch.empty(cap, dtype=torch.int32, device=dev)
+    ranges = torch.empty((T, 2), dtype=torch.int32, device=dev)
+    vis = torch.empty(max(N, 1), dtype=torch.uint8, device=dev)[:N]
+    overflow = torch.zeros(1, dtype=torch.int32, device=dev)
+    with timed("raster_render"):
+        _lib.check(L.cvhrf_raster_forward_render_capacity(ctypes.byref(sc), _p(geom), gbytes, _p(counts), cap,
+                                                          _p(binws), bbytes, _p(field), _p(final_Ts), _p(n_contrib),
+                                                          _p(point_list), _p(ranges), _p(vis), _p(overflow), st),
+                   "cvhrf_raster_forward_render_capacity")
+    last_counts = counts
+    info = dict(geom=geom, gbytes=gbytes, binws=binws, bbytes=bbytes, num_pairs=cap, final_Ts=final_Ts,
+                n_contrib=n_contrib, point_list=point_list, ranges=ranges, visible=vis, img=(W, H), cam=camp,
+                counts=counts, overflow=overflow)
     return field, info
 
 
@@ -153,6 +190,37 @@ class SplatTileCuda(torch.autograd.Function):
         cam, z, q, s, col, ph, op, pp, view = ctx.saved_tensors
         grads = rasterize_backward(grad_output, cam, z, q, s, col, ph, op, pp, view, ctx.info)
         return grads + (None,) * 9
+
+
+class SplatTileCudaCapacity(torch.autograd.Function):
+    """SplatTileCuda without host synchronisation (CUDA-graph capturable).
+
+    Extra last argument `pairs_capacity`; returns (field, visible_mask) where visible_mask
+    is uint8 per Gaussian.  The tensor `ctx`-independent overflow flag of the latest call
+    is `rasterizer.last_overflow` (device int32, 1 = capacity exceeded, outputs invalid)."""
+
+    @staticmethod
+    def forward(ctx, cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs,
+                fx, fy, px, py, view_matrix, img_size, near_plane, far_plane, pairs_capacity):
+        global last_overflow
+        field, info = rasterize_forward(cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs,
+                                        fx, fy, px, py, view_matrix, img_size, near_plane, far_plane,
+                                        pairs_capacity=pairs_capacity)
+        ctx.save_for_backward(cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs,
+                              view_matrix)
+        ctx.info = info
+        last_overflow = info["overflow"]
+        ctx.mark_non_differentiable(info["visible"])
+        return field, info["visible"]
+
+    @staticmethod
+    def backward(ctx, grad_output, grad_visible=None):
+        cam, z, q, s, col, ph, op, pp, view = ctx.saved_tensors
+        grads = rasterize_backward(grad_output, cam, z, q, s, col, ph, op, pp, view, ctx.info)
+        return grads + (None,) * 9
+
+
+last_overflow = None
 
 
 def splat_tile_cuda(cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs,

@@ -11,6 +11,13 @@ planes at linspace(-V/2, V/2, K) + d_val (V = 4 mm, d_val = -2 mm -> -4, -2, 0 m
 K = 3), each plane propagated by -d_p (model.py:1259), pad_size = aperture = max(W, H),
 pixel pitch 8 um (the config's value; the script default is 3.74 um).
 
+``capture()`` records one whole iteration (forward, backward, optimizer) in a CUDA graph
+through the host-synchronisation-free rasterizer path (fixed pair capacity, visibility as
+a row mask); ``replay()`` then runs an iteration with a single graph launch.  A device
+flag records whether any replayed iteration needed more pairs than the capacity
+(``graph_overflowed()``); such an iteration's outputs are invalid and the caller
+re-captures with a larger capacity.
+
 The reference optimizer receives the rasterizer's ``visible_indices``, which index the
 depth-sorted subset, not the parameter rows; here they are mapped back through the
 sort permutation (``idxs[visible]``) so the update lands on the rows that were seen.
@@ -20,7 +27,8 @@ import torch
 from . import scene as SC
 from .optimizer import SparseGaussianAdam
 from .propagation import propagate_planes
-from .rasterizer import splat_tile_cuda
+from . import rasterizer as RZ
+from .rasterizer import SplatTileCudaCapacity, splat_tile_cuda
 
 WAVELENGTHS = [639e-9, 532e-9, 473e-9]
 
@@ -66,3 +74,60 @@ class HoloTrainer:
         loss.backward()
         self.opt.step(visible)
         return loss.detach()
+
+    # ---- CUDA-graph mode ------------------------------------------------------------
+    def _forward_capacity(self, target):
+        kw, idxs = SC.render_inputs_fused(self.params, self.camera)
+        field, vis_mask = SplatTileCudaCapacity.apply(*SC.splat_args(kw), self.pairs_capacity)
+        holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
+        loss = ((holo.real.square() + holo.imag.square() - target) ** 2).mean()
+        n = self.params["means"].shape[0]
+        row_mask = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        row_mask.scatter_(0, idxs, vis_mask)
+        torch.maximum(self._overflow_acc, RZ.last_overflow, out=self._overflow_acc)
+        return loss, row_mask
+
+    def _step_capacity(self, exchange=None):
+        for p in self.params.values():
+            p.grad = None
+        loss, row_mask = self._forward_capacity(self._static_target)
+        loss.backward()
+        if exchange is not None:
+            row_mask = exchange(self, row_mask)
+        self.opt.step(row_mask=row_mask)
+        return loss.detach()
+
+    def capture(self, headroom=1.5, exchange=None, warmup=2, eager_step=None):
+        """Capture one iteration in a CUDA graph (runs `warmup` + 1 eager iterations first,
+        which train like normal steps).  The pair capacity is `headroom` x the pair count
+        of an eager iteration.  `exchange(trainer, row_mask) -> row_mask` is called between
+        backward and optimizer (the data-parallel gradient exchange); `eager_step` replaces
+        the first (eager) iteration, e.g. with its data-parallel form."""
+        (eager_step or self.step)()
+        self.pairs_capacity = int(RZ.last_num_pairs * headroom) + 4096
+        self._static_target = self.target.clone()
+        self._overflow_acc = torch.zeros(1, dtype=torch.int32, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._step_capacity(exchange)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self._overflow_acc.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        launches0 = RZ._lib.lib().cvhrf_kernel_launch_count()
+        with torch.cuda.graph(self.graph):
+            self._static_loss = self._step_capacity(exchange)
+        self.graph_launches = RZ._lib.lib().cvhrf_kernel_launch_count() - launches0
+        return self
+
+    def replay(self, target=None):
+        """One iteration through the captured graph; returns the (static) loss tensor."""
+        if target is not None:
+            self._static_target.copy_(target, non_blocking=True)
+        self.graph.replay()
+        return self._static_loss
+
+    def graph_overflowed(self):
+        """True if any replay since capture exceeded the pair capacity (synchronises)."""
+        return bool(self._overflow_acc.item())

@@ -173,6 +173,21 @@ int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, const void* geo
                                 int32_t* ranges, int64_t* visible_indices, void* stream);
 
 /*
+ * Forward phase 2 without the host round trip (for CUDA-graph capture): identical
+ * outputs, but the pair count stays on the device (counts_dev[0] from
+ * cvhrf_raster_forward_geometry), point_list / the binning workspace are sized for
+ * pairs_capacity, visibility is returned as a per-Gaussian uint8 mask (N) instead of
+ * compacted indices, and *overflow (device int32, caller-zeroed) is set to 1 when the
+ * count exceeds the capacity -- then nothing is rendered and the call must be repeated
+ * with a larger capacity.  The backward takes num_pairs = pairs_capacity.
+ */
+int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
+                                         const int32_t* counts_dev, int pairs_capacity, void* bin_ws,
+                                         size_t bin_bytes, void* field, float* final_Ts, int32_t* n_contrib,
+                                         int32_t* point_list, int32_t* ranges, uint8_t* visible_mask,
+                                         int32_t* overflow, void* stream);
+
+/*
  * Backward (replaces rasterizer_splat.cu:551-684, renderBackwardTileKernel and the
  * geometry backward): atomic-free — each tile writes one gradient record per
  * (tile, Gaussian) pair, then one thread per Gaussian reduces its records and
