@@ -7,8 +7,8 @@
 // order gives each Gaussian's contiguous slot range for its (tile, Gaussian) pairs.
 // Phase 2 (render): pairs are emitted in (depth, index) order and stably sorted by
 // tile, which reproduces the reference's (tile | depth) 64-bit key order exactly;
-// then one CTA per 16x16 tile composites all K planes in a single pass over the
-// tile's Gaussian list (the reference makes one pass per plane).
+// then one CTA per 16x16 tile composites the K planes one after another, each over the
+// tile's Gaussians of that plane (compacted on chip from the depth-ordered list).
 #include "raster_ws.cuh"
 
 namespace cvhrf {
@@ -137,144 +137,170 @@ __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32
 
 // renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
 //
-// 128 threads per 16x16 tile; each thread owns two horizontally adjacent pixels and
-// evaluates both with packed f32x2 arithmetic (sm_100 FFMA2/FMUL2/FADD2).  Every lane
-// of a packed operation is an ordinary IEEE-rounded float operation, so each pixel
-// sees the reference's arithmetic: power = -0.5 (dx (i00 dx + i10 dy) + dy (i01 dx +
-// i11 dy)), G = expf(power), alpha = min(0.99, (o G) w), T' = T (1 - alpha), done when
-// T' < 1e-4, last = 1-based position of the last contributor.  A pixel that is done or
-// outside the image contributes through a zero weight (acc + 0 * c == acc).
-template <int K, int C>
-__global__ void __launch_bounds__(128) render_forward_kernel(
+// One CTA of 64 threads per 16x16 tile; each thread owns four horizontally adjacent
+// pixels as two packed f32x2 pairs (sm_100 FFMA2/FMUL2/FADD2; every lane of a packed
+// operation is an ordinary IEEE-rounded float operation).  The planes are composited
+// one after another: for plane p the CTA walks the tile's depth-ordered list in batches
+// of 128, keeps (ballot compaction, order preserved) only the Gaussians whose plane-p
+// weight is >= the cutoff, and front-to-back blends them.  Per pixel this is exactly the
+// reference's chain: power = -0.5 (dx (i00 dx + i10 dy) + dy (i01 dx + i11 dy)),
+// skip if power > 0, G = expf(power), alpha = min(0.99, (o G) w), the pixel takes
+// colour * alpha * T, T' = T (1 - alpha), last = 1-based list position, and stops once
+// T' < 1e-4.  "Stopped" is the same as T < 1e-4 (T starts at 1 and changes only
+// through a contribution), so a stopped or off-image pixel just gets alpha = 0: then
+// T (1 - 0) == T and acc + 0 * c == acc exactly.  A plane ends early when every pixel
+// of the tile has stopped in it.
+template <int C>
+__global__ void __launch_bounds__(64) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
-    const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs,
+    const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs, int K,
     int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
-  constexpr int NB = 128;  // Gaussians staged per batch
-  __shared__ float2 s_m[NB];       // mean
-  __shared__ float2 s_o[NB];       // (opacity, -)
+  constexpr int NT = 64, NB = 128;
+  __shared__ float4 s_mo[NB];      // (mx, mx, my, list position)
   __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
   __shared__ float4 s_c1[NB];      // (i10, i10, i11, i11)
-  __shared__ float s_w[K][NB];
-  __shared__ int s_pm[NB];           // planes with weight >= 1e-6 (bit p)
-  __shared__ float2 s_cp[C][NB];
+  __shared__ float4 s_ow[NB];      // (o, o, w, w)
+  __shared__ float4 s_col[C][NB];  // (re, re, im, im)
+  __shared__ int s_cnt[4];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
-  const int lx = (threadIdx.x & 7) * 2, ly = threadIdx.x >> 3;
-  const int px = tx * kTile + lx, py = ty * kTile + ly;
-  const bool in0 = px < W && py < H, in1 = px + 1 < W && py < H;
-  const float2 npx = make_float2(-(float)px, -(float)(px + 1));
+  const int px = tx * kTile + (tid & 3) * 4, py = ty * kTile + (tid >> 2);
+  const bool rowin = py < H;
+  const float2 npxA = make_float2(-(float)px, -(float)(px + 1));
+  const float2 npxB = make_float2(-(float)(px + 2), -(float)(px + 3));
   const float pyf = (float)py;
   const int2 range = ranges[tile];
   const int n = range.y - range.x;
+  const size_t HW = (size_t)H * W, pix = (size_t)py * W + px;
 
-  float2 T[K];
-  int last0[K], last1[K];
-  bool done0[K], done1[K];
-  float2 acc0[K][C], acc1[K][C];
-#pragma unroll
   for (int p = 0; p < K; ++p) {
-    T[p] = make_float2(1.0f, 1.0f);
-    last0[p] = last1[p] = 0;
-    done0[p] = !in0;
-    done1[p] = !in1;
+    // off-image pixels start "stopped" (T = 0 < 1e-4) and are never written
+    float2 TA = make_float2(rowin && px < W ? 1.f : 0.f, rowin && px + 1 < W ? 1.f : 0.f);
+    float2 TB = make_float2(rowin && px + 2 < W ? 1.f : 0.f, rowin && px + 3 < W ? 1.f : 0.f);
+    int lA0 = 0, lA1 = 0, lB0 = 0, lB1 = 0;
+    float2 reA[C], imA[C], reB[C], imB[C];
 #pragma unroll
-    for (int c = 0; c < C; ++c) acc0[p][c] = acc1[p][c] = make_float2(0.f, 0.f);
-  }
-  bool alldone = !in0 && !in1;
+    for (int c = 0; c < C; ++c) reA[c] = imA[c] = reB[c] = imB[c] = make_float2(0.f, 0.f);
 
-  for (int base = 0; base < n; base += NB) {
-    if (__syncthreads_and(alldone)) break;
-    {
-      const int j = base + threadIdx.x;
-      if (j < n) {
-        const int gi = point_list[range.x + j];
-        const float4 r0 = rec0[gi];
-        const float4 cn = conic[gi];
-        s_m[threadIdx.x] = make_float2(r0.x, r0.y);
-        s_o[threadIdx.x] = make_float2(r0.z, r0.z);
-        s_c0[threadIdx.x] = make_float4(cn.x, cn.x, cn.y, cn.y);
-        s_c1[threadIdx.x] = make_float4(cn.z, cn.z, cn.w, cn.w);
-        int pm = 0;
+    for (int base = 0; base < n; base += NB) {
+      const bool mine_done = TA.x < 1e-4f && TA.y < 1e-4f && TB.x < 1e-4f && TB.y < 1e-4f;
+      if (__syncthreads_and(mine_done)) break;
+      // stage: keep this batch's plane-p Gaussians, in list order
+      int gi[2];
+      bool keep[2];
+      unsigned bal[2];
 #pragma unroll
-        for (int p = 0; p < K; ++p) {
-          const float w = plane_probs[gi * K + p];
-          s_w[p][threadIdx.x] = w;
-          pm |= (w >= kPlaneCutoff) ? (1 << p) : 0;
+      for (int r = 0; r < 2; ++r) {
+        const int j = base + r * NT + tid;
+        keep[r] = false;
+        gi[r] = 0;
+        if (j < n) {
+          gi[r] = point_list[range.x + j];
+          keep[r] = plane_probs[(size_t)gi[r] * K + p] >= kPlaneCutoff;
         }
-        s_pm[threadIdx.x] = pm;
-#pragma unroll
-        for (int c = 0; c < C; ++c) s_cp[c][threadIdx.x] = cp[gi * C + c];
+        bal[r] = __ballot_sync(0xffffffffu, keep[r]);
+        if (lane == 0) s_cnt[r * 2 + warp] = __popc(bal[r]);
       }
-    }
-    __syncthreads();
-    const int cnt = min(NB, n - base);
-    for (int jj = 0; jj < cnt && !alldone; ++jj) {
-      const float2 m = s_m[jj];
-      const float2 dx = __fadd2_rn(make_float2(m.x, m.x), npx);
-      const float dys = m.y - pyf;
-      const float2 dy = make_float2(dys, dys);
-      const float4 c0 = s_c0[jj], c1 = s_c1[jj];
-      const float2 u = __ffma2_rn(make_float2(c0.x, c0.y), dx, __fmul2_rn(make_float2(c1.x, c1.y), dy));
-      const float2 v = __ffma2_rn(make_float2(c0.z, c0.w), dx, __fmul2_rn(make_float2(c1.z, c1.w), dy));
-      const float2 power = __fmul2_rn(make_float2(-0.5f, -0.5f), __ffma2_rn(dx, u, __fmul2_rn(dy, v)));
-      const bool ok0 = power.x <= 0.0f, ok1 = power.y <= 0.0f;
-      if (!ok0 && !ok1) continue;
-      const int pm = s_pm[jj];
-      if (pm == 0) continue;
-      const float2 og = __fmul2_rn(s_o[jj], make_float2(expf(power.x), expf(power.y)));
-      const int pos = base + jj + 1;
-      bool flip = false;
+      __syncthreads();
+      const int c0 = s_cnt[0], c1 = s_cnt[1], c2 = s_cnt[2], c3 = s_cnt[3];
+      const unsigned lt = (1u << lane) - 1u;
 #pragma unroll
-      for (int p = 0; p < K; ++p) {
-        if (pm & (1 << p)) {
-          const float w = s_w[p][jj];
-          const bool a0 = ok0 && !done0[p], a1 = ok1 && !done1[p];
-          if (a0 || a1) {
-            const float2 aw = __fmul2_rn(og, make_float2(w, w));
-            const float2 alpha = make_float2(fminf(kMaxAlpha, aw.x), fminf(kMaxAlpha, aw.y));
-            const float2 test = __fmul2_rn(T[p], __fadd2_rn(make_float2(1.0f, 1.0f), make_float2(-alpha.x, -alpha.y)));
-            const float2 wt = __fmul2_rn(alpha, T[p]);
-            const float2 wt0 = make_float2(a0 ? wt.x : 0.f, a0 ? wt.x : 0.f);
-            const float2 wt1 = make_float2(a1 ? wt.y : 0.f, a1 ? wt.y : 0.f);
+      for (int r = 0; r < 2; ++r) {
+        if (keep[r]) {
+          const int seg = r * 2 + warp;
+          const int off = (seg > 0 ? c0 : 0) + (seg > 1 ? c1 : 0) + (seg > 2 ? c2 : 0) + __popc(bal[r] & lt);
+          const int g = gi[r];
+          const float4 r0 = rec0[g];
+          const float4 cn = conic[g];
+          const float w = plane_probs[(size_t)g * K + p];
+          s_mo[off] = make_float4(r0.x, r0.x, r0.y, __int_as_float(base + r * NT + tid + 1));
+          s_c0[off] = make_float4(cn.x, cn.x, cn.y, cn.y);
+          s_c1[off] = make_float4(cn.z, cn.z, cn.w, cn.w);
+          s_ow[off] = make_float4(r0.z, r0.z, w, w);
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-              const float2 col = s_cp[c][jj];
-              acc0[p][c] = __ffma2_rn(wt0, col, acc0[p][c]);
-              acc1[p][c] = __ffma2_rn(wt1, col, acc1[p][c]);
-            }
-            if (a0) { T[p].x = test.x; last0[p] = pos; if (test.x < 0.0001f) { done0[p] = true; flip = true; } }
-            if (a1) { T[p].y = test.y; last1[p] = pos; if (test.y < 0.0001f) { done1[p] = true; flip = true; } }
+          for (int c = 0; c < C; ++c) {
+            const float2 v = cp[(size_t)g * C + c];
+            s_col[c][off] = make_float4(v.x, v.x, v.y, v.y);
           }
         }
       }
-      if (flip) {
-        bool all = true;
+      __syncthreads();
+      const int cnt = c0 + c1 + c2 + c3;
+      for (int jj = 0; jj < cnt; ++jj) {
+        const float4 mo = s_mo[jj];
+        const float4 k0 = s_c0[jj], k1 = s_c1[jj];
+        const float2 mx = make_float2(mo.x, mo.y);
+        const float dys = mo.z - pyf;
+        const float2 dy = make_float2(dys, dys);
+        const float2 t1 = __fmul2_rn(make_float2(k1.x, k1.y), dy);
+        const float2 t2 = __fmul2_rn(make_float2(k1.z, k1.w), dy);
+        const float2 dxA = __fadd2_rn(mx, npxA), dxB = __fadd2_rn(mx, npxB);
+        const float2 uA = __ffma2_rn(make_float2(k0.x, k0.y), dxA, t1);
+        const float2 vA = __ffma2_rn(make_float2(k0.z, k0.w), dxA, t2);
+        const float2 uB = __ffma2_rn(make_float2(k0.x, k0.y), dxB, t1);
+        const float2 vB = __ffma2_rn(make_float2(k0.z, k0.w), dxB, t2);
+        const float2 nh = make_float2(-0.5f, -0.5f);
+        const float2 pA = __fmul2_rn(nh, __ffma2_rn(dxA, uA, __fmul2_rn(dy, vA)));
+        const float2 pB = __fmul2_rn(nh, __ffma2_rn(dxB, uB, __fmul2_rn(dy, vB)));
+        const bool aA0 = pA.x <= 0.f && !(TA.x < 1e-4f), aA1 = pA.y <= 0.f && !(TA.y < 1e-4f);
+        const bool aB0 = pB.x <= 0.f && !(TB.x < 1e-4f), aB1 = pB.y <= 0.f && !(TB.y < 1e-4f);
+        const float4 ow = s_ow[jj];
+        const float2 o2 = make_float2(ow.x, ow.y), w2 = make_float2(ow.z, ow.w);
+        const float2 awA = __fmul2_rn(__fmul2_rn(o2, make_float2(expf(pA.x), expf(pA.y))), w2);
+        const float2 awB = __fmul2_rn(__fmul2_rn(o2, make_float2(expf(pB.x), expf(pB.y))), w2);
+        const float2 alA = make_float2(aA0 ? fminf(kMaxAlpha, awA.x) : 0.f, aA1 ? fminf(kMaxAlpha, awA.y) : 0.f);
+        const float2 alB = make_float2(aB0 ? fminf(kMaxAlpha, awB.x) : 0.f, aB1 ? fminf(kMaxAlpha, awB.y) : 0.f);
+        const float2 one = make_float2(1.f, 1.f);
+        const float2 wtA = __fmul2_rn(alA, TA), wtB = __fmul2_rn(alB, TB);
+        TA = __fmul2_rn(TA, __fadd2_rn(one, make_float2(-alA.x, -alA.y)));
+        TB = __fmul2_rn(TB, __fadd2_rn(one, make_float2(-alB.x, -alB.y)));
 #pragma unroll
-        for (int p = 0; p < K; ++p) all = all && done0[p] && done1[p];
-        alldone = all;
+        for (int c = 0; c < C; ++c) {
+          const float4 col = s_col[c][jj];
+          const float2 cr = make_float2(col.x, col.y), ci = make_float2(col.z, col.w);
+          reA[c] = __ffma2_rn(wtA, cr, reA[c]);
+          imA[c] = __ffma2_rn(wtA, ci, imA[c]);
+          reB[c] = __ffma2_rn(wtB, cr, reB[c]);
+          imB[c] = __ffma2_rn(wtB, ci, imB[c]);
+        }
+        const int pos = __float_as_int(mo.w);
+        lA0 = aA0 ? pos : lA0;
+        lA1 = aA1 ? pos : lA1;
+        lB0 = aB0 ? pos : lB0;
+        lB1 = aB1 ? pos : lB1;
       }
     }
-  }
-  const size_t HW = (size_t)H * W, pix = (size_t)py * W + px;
+    if (rowin) {
+      const float Tv[4] = {TA.x, TA.y, TB.x, TB.y};
+      const int lv[4] = {lA0, lA1, lB0, lB1};
 #pragma unroll
-  for (int p = 0; p < K; ++p) {
+      for (int c = 0; c < C; ++c) {
+        const float re[4] = {reA[c].x, reA[c].y, reB[c].x, reB[c].y};
+        const float im[4] = {imA[c].x, imA[c].y, imB[c].x, imB[c].y};
+        float2* out = field + (size_t)(p * C + c) * HW + pix;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      if (in0) field[(p * C + c) * HW + pix] = acc0[p][c];
-      if (in1) field[(p * C + c) * HW + pix + 1] = acc1[p][c];
+        for (int q = 0; q < 4; ++q)
+          if (px + q < W) out[q] = make_float2(re[q], im[q]);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (px + q < W) {
+          final_T[p * HW + pix + q] = Tv[q];
+          n_contrib[p * HW + pix + q] = lv[q];
+        }
+      }
     }
-    if (in0) { final_T[p * HW + pix] = T[p].x; n_contrib[p * HW + pix] = last0[p]; }
-    if (in1) { final_T[p * HW + pix + 1] = T[p].y; n_contrib[p * HW + pix + 1] = last1[p]; }
+    __syncthreads();   // s_* are restaged by the next plane
   }
 }
 
-template <int K>
-int launch_render_k(int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
-                    const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
+int launch_render(int K, int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
+                  const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
   switch (C) {
-    case 1: render_forward_kernel<K, 1><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
-    case 2: render_forward_kernel<K, 2><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
-    default: render_forward_kernel<K, 3><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, W, H, gx, field, fT, nc); break;
+    case 1: render_forward_kernel<1><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
+    case 2: render_forward_kernel<2><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
+    default: render_forward_kernel<3><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
@@ -378,16 +404,8 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
   dim3 grid(T);
   const int2* rg = (const int2*)ranges;
   float2* f = (float2*)field;
-  switch (s.K) {
-    case 1: return launch_render_k<1>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 2: return launch_render_k<2>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 3: return launch_render_k<3>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 4: return launch_render_k<4>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 5: return launch_render_k<5>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 6: return launch_render_k<6>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 7: return launch_render_k<7>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    default: return launch_render_k<8>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-  }
+  return launch_render(s.K, s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts,
+                       n_contrib);
 }
 
 // Same as cvhrf_raster_forward_render without the host round trip: the pair count stays in
@@ -439,14 +457,6 @@ extern "C" int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* sc
   dim3 grid(T);
   const int2* rg = (const int2*)ranges;
   float2* f = (float2*)field;
-  switch (s.K) {
-    case 1: return launch_render_k<1>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 2: return launch_render_k<2>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 3: return launch_render_k<3>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 4: return launch_render_k<4>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 5: return launch_render_k<5>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 6: return launch_render_k<6>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    case 7: return launch_render_k<7>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-    default: return launch_render_k<8>(s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts, n_contrib);
-  }
+  return launch_render(s.K, s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts,
+                       n_contrib);
 }
