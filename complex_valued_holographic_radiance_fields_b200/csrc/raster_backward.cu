@@ -71,63 +71,88 @@ struct BwdG {
   float E, G;
 };
 
-// Per-pixel state of one plane's back-to-front replay (backward_splat.cu:133-148).  The
-// reference updates the accumulated colour lazily, at the next contributor, from the
-// previous contributor's alpha and colour; applying that same update right after each
-// contributor gives identical values and needs no last-alpha / last-colour registers.
+// Per-thread state of one plane's back-to-front replay for a horizontal pixel pair
+// (backward_splat.cu:133-148), packed per component: .x = left pixel, .y = right pixel.
+// The reference updates the accumulated colour lazily, at the next contributor, from
+// the previous contributor's alpha and colour; applying that same update right after
+// each contributor gives identical values and needs no last-alpha / last-colour state.
 template <int C>
-struct PixState {
-  float T;                        // transmittance
-  int last;                       // n_contrib: positions >= last are skipped
-  float2 dL[C], acc[C];           // dL/dpixel, accumulated colour behind
+struct PairState {
+  float2 T;                       // transmittance
+  int last0, last1;               // n_contrib: positions >= last are skipped
+  float2 dre[C], dim[C];          // dL/dpixel (real, imaginary)
+  float2 are[C], aim[C];          // accumulated colour behind (real, imaginary)
 };
 
-// One pixel, one Gaussian: renderBackwardTileKernel's arithmetic (:184-300), adding this
-// pixel's gradient contributions into v (6 + 1 + 2C entries).
+// Number of per-pixel sums reduced over the CTA for one Gaussian.  The reference's
+// per-pixel gradient terms (backward_splat.cu:236-300) are linear in
+//   gd = G dL/dalpha   (dL/dalpha already scaled by T)
+// and its products with the pixel offset d, so the CTA reduces
+//   S0 = sum gd, S1 = sum gd dx, S2 = sum gd dy, S3 = sum gd dx dx, S4 = sum gd dx dy,
+//   S5 = sum gd dy dy, colour_c = sum dch (cos dLre + sin dLim),
+//   phase_c = sum dch (-im(cp) dLre + re(cp) dLim)
+// and applies the per-Gaussian factors once (pair_record): with ow = opacity w,
+//   dmean = -ddel * ow (conic . (S1, S2)),  dconic = -0.5 ow (S3, S4, S5),
+//   dopacity = w S0,  dplane = opacity S0.
 template <int C>
-__device__ __forceinline__ void bwd_pixel(PixState<C>& st, const BwdG& g, float w, float2 d,
-                                          const float2* cpx, const float2* cs, float ddelx_dx, float ddely_dy,
-                                          float* v) {
-  const float power = -0.5f * (g.cx * d.x * d.x + g.cz * d.y * d.y) - g.cy * d.x * d.y;
-  if (power > 0.0f) return;
-  const float G = expf(power);
-  const float alpha = min(0.99f, g.opacity * G * w);
-  if (alpha < 1.0f / 255.0f) return;
-  st.T = st.T / (1.0f - alpha);
-  const float dch = alpha * st.T;
-  const float2 a2 = make_float2(alpha, alpha);
-  const float2 na2 = make_float2(1.0f - alpha, 1.0f - alpha);
-  float dL_dalpha = 0.0f;
+constexpr int red_len() { return 6 + 2 * C; }
+
+// One pixel pair, one Gaussian: renderBackwardTileKernel's per-pixel arithmetic
+// (:184-300) for both pixels at once; r[] receives the pair's share of the sums above.
+// A pixel that does not contribute (masked, power > 0, alpha < 1/255) gets alpha = 0 and
+// dL/dalpha = 0, which leaves its state unchanged exactly (T / 1, 0 c + 1 acc) and adds
+// exact zeros.
+template <int C>
+__device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float w, float2 dx, float dy, bool n0,
+                                         bool n1, const float4* cpx, const float4* cs, float* r) {
+  const float2 dy2 = make_float2(dy, dy);
+  const float2 cx2 = make_float2(g.cx, g.cx);
+  const float czdd = g.cz * dy * dy;
+  const float ncydy = -(g.cy * dy);
+  const float2 quad = __ffma2_rn(__fmul2_rn(cx2, dx), dx, make_float2(czdd, czdd));
+  const float2 power = __ffma2_rn(make_float2(-0.5f, -0.5f), quad, __fmul2_rn(make_float2(ncydy, ncydy), dx));
+  const float2 G = make_float2(expf(power.x), expf(power.y));
+  const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(g.opacity, g.opacity), G), make_float2(w, w));
+  const float al0 = fminf(0.99f, aw.x), al1 = fminf(0.99f, aw.y);
+  const bool a0 = n0 && power.x <= 0.0f && al0 >= 1.0f / 255.0f;
+  const bool a1 = n1 && power.y <= 0.0f && al1 >= 1.0f / 255.0f;
+  const float2 al = make_float2(a0 ? al0 : 0.f, a1 ? al1 : 0.f);
+  const float2 om = make_float2(1.0f - al.x, 1.0f - al.y);
+  st.T = make_float2(__fdividef(st.T.x, om.x), __fdividef(st.T.y, om.y));
+  const float2 dch = __fmul2_rn(al, st.T);
+  float2 dLda = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    const float2 t = __fmul2_rn(__fadd2_rn(cpx[c], make_float2(-st.acc[c].x, -st.acc[c].y)), st.dL[c]);
-    dL_dalpha += t.x;
-    dL_dalpha += t.y;
-    v[7 + c] += dch * (cs[c].x * st.dL[c].x + cs[c].y * st.dL[c].y);
-    v[7 + C + c] += dch * (-cpx[c].y * st.dL[c].x + cpx[c].x * st.dL[c].y);
-    st.acc[c] = __ffma2_rn(a2, cpx[c], __fmul2_rn(na2, st.acc[c]));
+    const float2 cr = make_float2(cpx[c].x, cpx[c].y), ci = make_float2(cpx[c].z, cpx[c].w);
+    dLda = __ffma2_rn(__fadd2_rn(cr, make_float2(-st.are[c].x, -st.are[c].y)), st.dre[c], dLda);
+    dLda = __ffma2_rn(__fadd2_rn(ci, make_float2(-st.aim[c].x, -st.aim[c].y)), st.dim[c], dLda);
+    const float2 sc = __ffma2_rn(make_float2(cs[c].z, cs[c].w), st.dim[c],
+                                 __fmul2_rn(make_float2(cs[c].x, cs[c].y), st.dre[c]));
+    const float2 sp = __ffma2_rn(cr, st.dim[c], __fmul2_rn(make_float2(-ci.x, -ci.y), st.dre[c]));
+    const float2 vc = __fmul2_rn(dch, sc), vp = __fmul2_rn(dch, sp);
+    r[6 + c] = vc.x + vc.y;
+    r[6 + C + c] = vp.x + vp.y;
+    st.are[c] = __ffma2_rn(al, cr, __fmul2_rn(om, st.are[c]));
+    st.aim[c] = __ffma2_rn(al, ci, __fmul2_rn(om, st.aim[c]));
   }
-  dL_dalpha *= st.T;
-  const float dL_dG = g.opacity * w * dL_dalpha;
-  const float gdx = G * d.x, gdy = G * d.y;
-  v[0] += dL_dG * (-gdx * g.cx - gdy * g.cy) * ddelx_dx;
-  v[1] += dL_dG * (-gdy * g.cz - gdx * g.cy) * ddely_dy;
-  const float dcx = -0.5f * gdx * d.x * dL_dG;
-  const float dcy = -0.5f * gdx * d.y * dL_dG;
-  const float dcz = -0.5f * gdy * d.y * dL_dG;
-  v[2] += dcx * g.A + dcz * g.B;
-  v[3] += dcx * g.Cc + dcy * g.D + dcz * g.E;
-  v[4] += dcx * g.B + dcz * g.G;
-  v[5] += G * w * dL_dalpha;
-  v[6] += g.opacity * G * dL_dalpha;
+  dLda = __fmul2_rn(dLda, st.T);
+  const float2 gd = make_float2(a0 ? G.x * dLda.x : 0.f, a1 ? G.y * dLda.y : 0.f);
+  const float2 gdx = __fmul2_rn(gd, dx), gdy = __fmul2_rn(gd, dy2);
+  const float2 gdxx = __fmul2_rn(gdx, dx), gdxy = __fmul2_rn(gdx, dy2), gdyy = __fmul2_rn(gdy, dy2);
+  r[0] = gd.x + gd.y;
+  r[1] = gdx.x + gdx.y;
+  r[2] = gdy.x + gdy.y;
+  r[3] = gdxx.x + gdxx.y;
+  r[4] = gdxy.x + gdxy.y;
+  r[5] = gdyy.x + gdyy.y;
 }
 
 // One CTA per 16x16 tile, 128 threads x 2 horizontally adjacent pixels, one pass per
 // plane.  Each pass stages the tile list back to front in batches, keeps only the
 // Gaussians that can contribute on this plane inside this tile (plane weight >= 1e-6,
 // alpha >= 1/255 box meets the tile, position below the tile's largest n_contrib), and
-// for each of those reduces the per-pixel contributions over the CTA into the pair's
-// record (records start at zero; each pass adds its plane's share).
+// for each of those reduces the per-pixel sums over the CTA and adds the pair's share
+// into its record (records start at zero; each pass adds its plane's share).
 template <int C>
 __global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
@@ -135,14 +160,14 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
     float* __restrict__ records) {
-  constexpr int NB = 128, NW = 4;
-  static_assert(7 + 2 * C <= kRedV, "reduction vector too long");
+  constexpr int NB = 128, NW = 4, RL = red_len<C>();
+  static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
   __shared__ int s_pos[NB];
   __shared__ BwdG s_g[NB];
   __shared__ float s_w[NB];
-  __shared__ float2 s_cpx[C][NB];
-  __shared__ float2 s_cs[C][NB];
+  __shared__ float4 s_cpx[C][NB];   // (re, re, im, im) of colour * e^{i phase}
+  __shared__ float4 s_cs[C][NB];    // (cos, cos, sin, sin)
   __shared__ float s_part[NW][32][kRedV];
   __shared__ int s_wcnt[NW];
   __shared__ int s_maxlast;
@@ -153,7 +178,8 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int px = tx * kTile + (threadIdx.x & 7) * 2, py = ty * kTile + (threadIdx.x >> 3);
   const bool in0 = px < W && py < H, in1 = px + 1 < W && py < H;
-  const float2 p0f = make_float2((float)px, (float)py), p1f = make_float2((float)(px + 1), (float)py);
+  const float2 npx = make_float2(-(float)px, -(float)(px + 1));
+  const float pyf = (float)py;
   const int2 range = ranges[tile];
   const int n = range.y - range.x;
   if (n <= 0) return;
@@ -165,21 +191,22 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   const unsigned lt = (1u << lane) - 1u;
 
   for (int p = 0; p < K; ++p) {
-    PixState<C> s0, s1;
-    s0.T = in0 ? final_T[p * HW + pix0] : 0.f;
-    s1.T = in1 ? final_T[p * HW + pix1] : 0.f;
-    s0.last = in0 ? n_contrib[p * HW + pix0] : 0;
-    s1.last = in1 ? n_contrib[p * HW + pix1] : 0;
+    PairState<C> st;
+    st.T = make_float2(in0 ? final_T[p * HW + pix0] : 0.f, in1 ? final_T[p * HW + pix1] : 0.f);
+    st.last0 = in0 ? n_contrib[p * HW + pix0] : 0;
+    st.last1 = in1 ? n_contrib[p * HW + pix1] : 0;
 #pragma unroll
     for (int c = 0; c < C; ++c) {
-      s0.dL[c] = in0 ? grad_field[(size_t)(p * C + c) * HW + pix0] : make_float2(0.f, 0.f);
-      s1.dL[c] = in1 ? grad_field[(size_t)(p * C + c) * HW + pix1] : make_float2(0.f, 0.f);
-      s0.acc[c] = s1.acc[c] = make_float2(0.f, 0.f);
+      const float2 g0 = in0 ? grad_field[(size_t)(p * C + c) * HW + pix0] : make_float2(0.f, 0.f);
+      const float2 g1 = in1 ? grad_field[(size_t)(p * C + c) * HW + pix1] : make_float2(0.f, 0.f);
+      st.dre[c] = make_float2(g0.x, g1.x);
+      st.dim[c] = make_float2(g0.y, g1.y);
+      st.are[c] = st.aim[c] = make_float2(0.f, 0.f);
     }
     __syncthreads();
     if (threadIdx.x == 0) s_maxlast = 0;
     __syncthreads();
-    atomicMax(&s_maxlast, max(s0.last, s1.last));
+    atomicMax(&s_maxlast, max(st.last0, st.last1));
     __syncthreads();
     const int n_eff = min(n, s_maxlast);
 
@@ -241,8 +268,8 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           float sn, cs;
           __sincosf(phase[gi * C + c], &sn, &cs);
           const float col = colours[gi * C + c];
-          s_cs[c][idx] = make_float2(cs, sn);
-          s_cpx[c][idx] = make_float2(col * cs, col * sn);
+          s_cs[c][idx] = make_float4(cs, cs, sn, sn);
+          s_cpx[c][idx] = make_float4(col * cs, col * cs, col * sn, col * sn);
         }
       }
       __syncthreads();
@@ -253,41 +280,60 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           const int jj = jb + jl;
           const BwdG& gg = s_g[jj];
           const int q = s_pos[jj];
-          const float2 d0 = make_float2(gg.mx - p0f.x, gg.my - p0f.y);
-          const float2 d1 = make_float2(gg.mx - p1f.x, gg.my - p1f.y);
-          const bool ny = fabsf(d0.y) <= gg.ey;
-          const bool n0 = in0 && q < s0.last && ny && fabsf(d0.x) <= gg.ex;
-          const bool n1 = in1 && q < s1.last && ny && fabsf(d1.x) <= gg.ex;
+          const float2 dx = __fadd2_rn(make_float2(gg.mx, gg.mx), npx);
+          const float dy = gg.my - pyf;
+          const bool ny = fabsf(dy) <= gg.ey;
+          const bool n0 = in0 && q < st.last0 && ny && fabsf(dx.x) <= gg.ex;
+          const bool n1 = in1 && q < st.last1 && ny && fabsf(dx.y) <= gg.ex;
           if (!__any_sync(0xffffffffu, n0 || n1)) {
             if (lane < kRedV) s_part[warp][jl][lane] = 0.f;
             continue;
           }
           float v[kRedV];
-#pragma unroll
-          for (int i = 0; i < kRedV; ++i) v[i] = 0.f;
-          float2 cpx[C], cs[C];
+          float4 cpx[C], cs[C];
 #pragma unroll
           for (int c = 0; c < C; ++c) {
             cpx[c] = s_cpx[c][jj];
             cs[c] = s_cs[c][jj];
           }
-          const float ww = s_w[jj];
-          if (n0) bwd_pixel<C>(s0, gg, ww, d0, cpx, cs, ddelx_dx, ddely_dy, v);
-          if (n1) bwd_pixel<C>(s1, gg, ww, d1, cpx, cs, ddelx_dx, ddely_dy, v);
+          bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, cs, v);
+#pragma unroll
+          for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
           const float tot = warp_reduce_scatter16(v);
           if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
         }
         __syncthreads();
-        const int V = 7 + 2 * C;
-        for (int e = threadIdx.x; e < nj * kRedV; e += blockDim.x) {
-          const int jl = e / kRedV, idx = e - jl * kRedV;
-          if (idx >= V) continue;
+        // sums over the warps, in place into s_part[0]
+        for (int e = threadIdx.x; e < nj * RL; e += blockDim.x) {
+          const int jl = e / RL, idx = e - jl * RL;
           float sum = 0.f;
 #pragma unroll
           for (int w2 = 0; w2 < NW; ++w2) sum += s_part[w2][jl][idx];
+          s_part[0][jl][idx] = sum;
+        }
+        __syncthreads();
+        // the pair's record share: per-Gaussian factors applied once
+        const int VO = 7 + 2 * C;
+        for (int e = threadIdx.x; e < nj * VO; e += blockDim.x) {
+          const int jl = e / VO, idx = e - jl * VO;
+          const float* S = s_part[0][jl];
+          const BwdG& gg = s_g[jb + jl];
+          const float ww = s_w[jb + jl];
+          const float ow = gg.opacity * ww;
+          float val;
+          if (idx == 0) val = -ddelx_dx * ow * (gg.cx * S[1] + gg.cy * S[2]);
+          else if (idx == 1) val = -ddely_dy * ow * (gg.cz * S[2] + gg.cy * S[1]);
+          else if (idx <= 4) {
+            const float dcx = -0.5f * ow * S[3], dcy = -0.5f * ow * S[4], dcz = -0.5f * ow * S[5];
+            val = idx == 2 ? dcx * gg.A + dcz * gg.B
+                : idx == 3 ? dcx * gg.Cc + dcy * gg.D + dcz * gg.E
+                           : dcx * gg.B + dcz * gg.G;
+          } else if (idx == 5) val = ww * S[0];
+          else if (idx == 6) val = gg.opacity * S[0];
+          else val = S[idx - 1];   // colour, phase sums (S[6 ..])
           const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
           float* dst = records + (size_t)s_slot[jb + jl] * VR + ri;
-          *dst += sum;
+          *dst += val;
         }
         __syncthreads();
       }
