@@ -104,7 +104,7 @@ constexpr int red_len() { return 6 + 2 * C; }
 // exact zeros.
 template <int C>
 __device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float w, float2 dx, float dy, bool n0,
-                                         bool n1, const float4* cpx, const float4* cs, float* r) {
+                                         bool n1, const float4* cpx, const float2* cs, float* r) {
   const float2 dy2 = make_float2(dy, dy);
   const float2 cx2 = make_float2(g.cx, g.cx);
   const float czdd = g.cz * dy * dy;
@@ -126,8 +126,8 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float 
     const float2 cr = make_float2(cpx[c].x, cpx[c].y), ci = make_float2(cpx[c].z, cpx[c].w);
     dLda = __ffma2_rn(__fadd2_rn(cr, make_float2(-st.are[c].x, -st.are[c].y)), st.dre[c], dLda);
     dLda = __ffma2_rn(__fadd2_rn(ci, make_float2(-st.aim[c].x, -st.aim[c].y)), st.dim[c], dLda);
-    const float2 sc = __ffma2_rn(make_float2(cs[c].z, cs[c].w), st.dim[c],
-                                 __fmul2_rn(make_float2(cs[c].x, cs[c].y), st.dre[c]));
+    const float2 sc = __ffma2_rn(make_float2(cs[c].y, cs[c].y), st.dim[c],
+                                 __fmul2_rn(make_float2(cs[c].x, cs[c].x), st.dre[c]));
     const float2 sp = __ffma2_rn(cr, st.dim[c], __fmul2_rn(make_float2(-ci.x, -ci.y), st.dre[c]));
     const float2 vc = __fmul2_rn(dch, sc), vp = __fmul2_rn(dch, sp);
     r[6 + c] = vc.x + vc.y;
@@ -160,15 +160,15 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
     float* __restrict__ records) {
-  constexpr int NB = 128, NW = 4, RL = red_len<C>();
+  constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL + 1;
   static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
   __shared__ int s_pos[NB];
   __shared__ BwdG s_g[NB];
   __shared__ float s_w[NB];
   __shared__ float4 s_cpx[C][NB];   // (re, re, im, im) of colour * e^{i phase}
-  __shared__ float4 s_cs[C][NB];    // (cos, cos, sin, sin)
-  __shared__ float s_part[NW][32][kRedV];
+  __shared__ float2 s_cs[C][NB];    // (cos, sin)
+  __shared__ float s_part[NW][NB][RP];
   __shared__ int s_wcnt[NW];
   __shared__ int s_maxlast;
 
@@ -268,74 +268,63 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           float sn, cs;
           __sincosf(phase[gi * C + c], &sn, &cs);
           const float col = colours[gi * C + c];
-          s_cs[c][idx] = make_float4(cs, cs, sn, sn);
+          s_cs[c][idx] = make_float2(cs, sn);
           s_cpx[c][idx] = make_float4(col * cs, col * cs, col * sn, col * sn);
         }
       }
       __syncthreads();
-      // ---- replay the kept Gaussians, 32 at a time ----
-      for (int jb = 0; jb < total; jb += 32) {
-        const int nj = min(32, total - jb);
-        for (int jl = 0; jl < nj; ++jl) {
-          const int jj = jb + jl;
-          const BwdG& gg = s_g[jj];
-          const int q = s_pos[jj];
-          const float2 dx = __fadd2_rn(make_float2(gg.mx, gg.mx), npx);
-          const float dy = gg.my - pyf;
-          const bool ny = fabsf(dy) <= gg.ey;
-          const bool n0 = in0 && q < st.last0 && ny && fabsf(dx.x) <= gg.ex;
-          const bool n1 = in1 && q < st.last1 && ny && fabsf(dx.y) <= gg.ex;
-          if (!__any_sync(0xffffffffu, n0 || n1)) {
-            if (lane < kRedV) s_part[warp][jl][lane] = 0.f;
-            continue;
-          }
-          float v[kRedV];
-          float4 cpx[C], cs[C];
-#pragma unroll
-          for (int c = 0; c < C; ++c) {
-            cpx[c] = s_cpx[c][jj];
-            cs[c] = s_cs[c][jj];
-          }
-          bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, cs, v);
-#pragma unroll
-          for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
-          const float tot = warp_reduce_scatter16(v);
-          if ((lane & 1) == 0) s_part[warp][jl][lane >> 1] = tot;
+      // ---- each warp replays all kept Gaussians over its 16 x 4 pixels ----
+      for (int jj = 0; jj < total; ++jj) {
+        const BwdG& gg = s_g[jj];
+        const int q = s_pos[jj];
+        const float2 dx = __fadd2_rn(make_float2(gg.mx, gg.mx), npx);
+        const float dy = gg.my - pyf;
+        const bool ny = fabsf(dy) <= gg.ey;
+        const bool n0 = in0 && q < st.last0 && ny && fabsf(dx.x) <= gg.ex;
+        const bool n1 = in1 && q < st.last1 && ny && fabsf(dx.y) <= gg.ex;
+        if (!__any_sync(0xffffffffu, n0 || n1)) {
+          if (lane < RL) s_part[warp][jj][lane] = 0.f;
+          continue;
         }
-        __syncthreads();
-        // sums over the warps, in place into s_part[0]
-        for (int e = threadIdx.x; e < nj * RL; e += blockDim.x) {
-          const int jl = e / RL, idx = e - jl * RL;
-          float sum = 0.f;
+        float v[kRedV];
+        float4 cpx[C];
+        float2 cs[C];
 #pragma unroll
-          for (int w2 = 0; w2 < NW; ++w2) sum += s_part[w2][jl][idx];
-          s_part[0][jl][idx] = sum;
+        for (int c = 0; c < C; ++c) {
+          cpx[c] = s_cpx[c][jj];
+          cs[c] = s_cs[c][jj];
         }
-        __syncthreads();
-        // the pair's record share: per-Gaussian factors applied once
-        const int VO = 7 + 2 * C;
-        for (int e = threadIdx.x; e < nj * VO; e += blockDim.x) {
-          const int jl = e / VO, idx = e - jl * VO;
-          const float* S = s_part[0][jl];
-          const BwdG& gg = s_g[jb + jl];
-          const float ww = s_w[jb + jl];
-          const float ow = gg.opacity * ww;
-          float val;
-          if (idx == 0) val = -ddelx_dx * ow * (gg.cx * S[1] + gg.cy * S[2]);
-          else if (idx == 1) val = -ddely_dy * ow * (gg.cz * S[2] + gg.cy * S[1]);
-          else if (idx <= 4) {
-            const float dcx = -0.5f * ow * S[3], dcy = -0.5f * ow * S[4], dcz = -0.5f * ow * S[5];
-            val = idx == 2 ? dcx * gg.A + dcz * gg.B
-                : idx == 3 ? dcx * gg.Cc + dcy * gg.D + dcz * gg.E
-                           : dcx * gg.B + dcz * gg.G;
-          } else if (idx == 5) val = ww * S[0];
-          else if (idx == 6) val = gg.opacity * S[0];
-          else val = S[idx - 1];   // colour, phase sums (S[6 ..])
-          const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
-          float* dst = records + (size_t)s_slot[jb + jl] * VR + ri;
+        bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, cs, v);
+#pragma unroll
+        for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
+        const float tot = warp_reduce_scatter16(v);
+        if ((lane & 1) == 0 && (lane >> 1) < RL) s_part[warp][jj][lane >> 1] = tot;
+      }
+      __syncthreads();
+      // ---- the pair's record share: the warps' sums, per-Gaussian factors applied once ----
+      const int VO = 7 + 2 * C;
+      for (int e = threadIdx.x; e < total * VO; e += blockDim.x) {
+        const int j = e / VO, idx = e - j * VO;
+        float S[RL];
+#pragma unroll
+        for (int k = 0; k < 6; ++k) S[k] = s_part[0][j][k] + s_part[1][j][k] + s_part[2][j][k] + s_part[3][j][k];
+        const BwdG& gg = s_g[j];
+        const float ww = s_w[j];
+        const float ow = gg.opacity * ww;
+        float val;
+        if (idx == 0) val = -ddelx_dx * ow * (gg.cx * S[1] + gg.cy * S[2]);
+        else if (idx == 1) val = -ddely_dy * ow * (gg.cz * S[2] + gg.cy * S[1]);
+        else if (idx <= 4) {
+          const float dcx = -0.5f * ow * S[3], dcy = -0.5f * ow * S[4], dcz = -0.5f * ow * S[5];
+          val = idx == 2 ? dcx * gg.A + dcz * gg.B
+              : idx == 3 ? dcx * gg.Cc + dcy * gg.D + dcz * gg.E
+                         : dcx * gg.B + dcz * gg.G;
+        } else if (idx == 5) val = ww * S[0];
+        else if (idx == 6) val = gg.opacity * S[0];
+        else val = s_part[0][j][idx - 1] + s_part[1][j][idx - 1] + s_part[2][j][idx - 1] + s_part[3][j][idx - 1];
+        const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
+        float* dst = records + (size_t)s_slot[j] * VR + ri;
           *dst += val;
-        }
-        __syncthreads();
       }
     }
   }
@@ -437,6 +426,14 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
     CVHRF_CUDA_TRY(cudaMemsetAsync(rec, 0, (size_t)num_pairs * (6 + s.K + 2 * s.C) * sizeof(float), st));
     const int2* rg = (const int2*)ranges;
     const float2* gf = (const float2*)grad_field;
+    // five 45 KB CTAs per SM need the full shared-memory carve-out (set once, before any capture)
+    static const bool carve = [] {
+      cudaFuncSetAttribute(render_backward_kernel<1>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      cudaFuncSetAttribute(render_backward_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      cudaFuncSetAttribute(render_backward_kernel<3>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      return true;
+    }();
+    (void)carve;
 #define CVHRF_BWD(CC)                                                                                       \
   render_backward_kernel<CC><<<grid, 128, 0, st>>>(rg, pl, b.slot, g.rec0, g.cov2d, s.colours, s.phase,      \
                                                    s.plane_probs, final_Ts, n_contrib, gf, s.K, s.W, s.H,    \
