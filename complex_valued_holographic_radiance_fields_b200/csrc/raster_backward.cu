@@ -17,6 +17,12 @@
 
 namespace cvhrf {
 
+#ifdef CVHRF_BWD_STATS
+// debugging counters (not built into the library): kept Gaussians, warp iterations,
+// active warp iterations, candidate pixels, contributing pixels
+__device__ unsigned long long g_bwd_stats[8];
+#endif
+
 namespace {
 
 constexpr int kRedV = 16;  // padded length of the per-Gaussian vector that is reduced
@@ -73,38 +79,41 @@ struct BwdG {
 
 // Per-thread state of one plane's back-to-front replay for a horizontal pixel pair
 // (backward_splat.cu:133-148), packed per component: .x = left pixel, .y = right pixel.
-// The reference updates the accumulated colour lazily, at the next contributor, from
-// the previous contributor's alpha and colour; applying that same update right after
-// each contributor gives identical values and needs no last-alpha / last-colour state.
+// The reference keeps the colour accumulated behind the current Gaussian, acc_c, and
+// uses it only in dL/dalpha = sum_c (cp_c - acc_c) . dL_c (real dot product of the
+// complex components).  Only Q = sum_c acc_c . dL_c is therefore kept: with
+// P = sum_c cp_c . dL_c, dL/dalpha = P - Q and the update acc_c' = alpha cp_c +
+// (1 - alpha) acc_c becomes Q' = alpha P + (1 - alpha) Q.  (The reference applies the
+// update lazily at the next contributor; applying it right away gives the same values.)
 template <int C>
 struct PairState {
   float2 T;                       // transmittance
   int last0, last1;               // n_contrib: positions >= last are skipped
   float2 dre[C], dim[C];          // dL/dpixel (real, imaginary)
-  float2 are[C], aim[C];          // accumulated colour behind (real, imaginary)
+  float2 Q;                       // sum_c acc_c . dL_c
 };
 
 // Number of per-pixel sums reduced over the CTA for one Gaussian.  The reference's
 // per-pixel gradient terms (backward_splat.cu:236-300) are linear in
-//   gd = G dL/dalpha   (dL/dalpha already scaled by T)
-// and its products with the pixel offset d, so the CTA reduces
+//   gd = G dL/dalpha   (dL/dalpha already scaled by T)   and   dch = alpha T
+// times quantities that are either per-pixel (offset d, dL) or per-Gaussian, so the CTA
+// reduces
 //   S0 = sum gd, S1 = sum gd dx, S2 = sum gd dy, S3 = sum gd dx dx, S4 = sum gd dx dy,
-//   S5 = sum gd dy dy, colour_c = sum dch (cos dLre + sin dLim),
-//   phase_c = sum dch (-im(cp) dLre + re(cp) dLim)
-// and applies the per-Gaussian factors once (pair_record): with ow = opacity w,
+//   S5 = sum gd dy dy, X_c = sum dch re(dL_c), Y_c = sum dch im(dL_c)
+// and applies the per-Gaussian factors once per (tile, Gaussian): with ow = opacity w,
 //   dmean = -ddel * ow (conic . (S1, S2)),  dconic = -0.5 ow (S3, S4, S5),
-//   dopacity = w S0,  dplane = opacity S0.
+//   dopacity = w S0,  dplane = opacity S0,
+//   dcolour_c = cos X_c + sin Y_c,  dphase_c = -im(cp_c) X_c + re(cp_c) Y_c.
 template <int C>
 constexpr int red_len() { return 6 + 2 * C; }
 
 // One pixel pair, one Gaussian: renderBackwardTileKernel's per-pixel arithmetic
 // (:184-300) for both pixels at once; r[] receives the pair's share of the sums above.
 // A pixel that does not contribute (masked, power > 0, alpha < 1/255) gets alpha = 0 and
-// dL/dalpha = 0, which leaves its state unchanged exactly (T / 1, 0 c + 1 acc) and adds
-// exact zeros.
+// gd = 0, which leaves its state unchanged exactly (T / 1, 0 P + 1 Q) and adds exact zeros.
 template <int C>
 __device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float w, float2 dx, float dy, bool n0,
-                                         bool n1, const float4* cpx, const float2* cs, float* r) {
+                                         bool n1, const float4* cpx, float* r) {
   const float2 dy2 = make_float2(dy, dy);
   const float2 cx2 = make_float2(g.cx, g.cx);
   const float czdd = g.cz * dy * dy;
@@ -116,26 +125,31 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float 
   const float al0 = fminf(0.99f, aw.x), al1 = fminf(0.99f, aw.y);
   const bool a0 = n0 && power.x <= 0.0f && al0 >= 1.0f / 255.0f;
   const bool a1 = n1 && power.y <= 0.0f && al1 >= 1.0f / 255.0f;
+#ifdef CVHRF_BWD_STATS
+  {
+    const unsigned cand = __popc(__ballot_sync(0xffffffffu, n0)) + __popc(__ballot_sync(0xffffffffu, n1));
+    const unsigned act = __popc(__ballot_sync(0xffffffffu, a0)) + __popc(__ballot_sync(0xffffffffu, a1));
+    if ((threadIdx.x & 31) == 0) {
+      atomicAdd(&g_bwd_stats[3], (unsigned long long)cand);
+      atomicAdd(&g_bwd_stats[4], (unsigned long long)act);
+    }
+  }
+#endif
   const float2 al = make_float2(a0 ? al0 : 0.f, a1 ? al1 : 0.f);
   const float2 om = make_float2(1.0f - al.x, 1.0f - al.y);
   st.T = make_float2(__fdividef(st.T.x, om.x), __fdividef(st.T.y, om.y));
   const float2 dch = __fmul2_rn(al, st.T);
-  float2 dLda = make_float2(0.f, 0.f);
+  float2 P = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    const float2 cr = make_float2(cpx[c].x, cpx[c].y), ci = make_float2(cpx[c].z, cpx[c].w);
-    dLda = __ffma2_rn(__fadd2_rn(cr, make_float2(-st.are[c].x, -st.are[c].y)), st.dre[c], dLda);
-    dLda = __ffma2_rn(__fadd2_rn(ci, make_float2(-st.aim[c].x, -st.aim[c].y)), st.dim[c], dLda);
-    const float2 sc = __ffma2_rn(make_float2(cs[c].y, cs[c].y), st.dim[c],
-                                 __fmul2_rn(make_float2(cs[c].x, cs[c].x), st.dre[c]));
-    const float2 sp = __ffma2_rn(cr, st.dim[c], __fmul2_rn(make_float2(-ci.x, -ci.y), st.dre[c]));
-    const float2 vc = __fmul2_rn(dch, sc), vp = __fmul2_rn(dch, sp);
-    r[6 + c] = vc.x + vc.y;
-    r[6 + C + c] = vp.x + vp.y;
-    st.are[c] = __ffma2_rn(al, cr, __fmul2_rn(om, st.are[c]));
-    st.aim[c] = __ffma2_rn(al, ci, __fmul2_rn(om, st.aim[c]));
+    P = __ffma2_rn(make_float2(cpx[c].x, cpx[c].y), st.dre[c], P);
+    P = __ffma2_rn(make_float2(cpx[c].z, cpx[c].w), st.dim[c], P);
+    const float2 X = __fmul2_rn(dch, st.dre[c]), Y = __fmul2_rn(dch, st.dim[c]);
+    r[6 + c] = X.x + X.y;
+    r[6 + C + c] = Y.x + Y.y;
   }
-  dLda = __fmul2_rn(dLda, st.T);
+  const float2 dLda = __fmul2_rn(__fadd2_rn(P, make_float2(-st.Q.x, -st.Q.y)), st.T);
+  st.Q = __ffma2_rn(al, P, __fmul2_rn(om, st.Q));
   const float2 gd = make_float2(a0 ? G.x * dLda.x : 0.f, a1 ? G.y * dLda.y : 0.f);
   const float2 gdx = __fmul2_rn(gd, dx), gdy = __fmul2_rn(gd, dy2);
   const float2 gdxx = __fmul2_rn(gdx, dx), gdxy = __fmul2_rn(gdx, dy2), gdyy = __fmul2_rn(gdy, dy2);
@@ -201,8 +215,8 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
       const float2 g1 = in1 ? grad_field[(size_t)(p * C + c) * HW + pix1] : make_float2(0.f, 0.f);
       st.dre[c] = make_float2(g0.x, g1.x);
       st.dim[c] = make_float2(g0.y, g1.y);
-      st.are[c] = st.aim[c] = make_float2(0.f, 0.f);
     }
+    st.Q = make_float2(0.f, 0.f);
     __syncthreads();
     if (threadIdx.x == 0) s_maxlast = 0;
     __syncthreads();
@@ -274,6 +288,10 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
       }
       __syncthreads();
       // ---- each warp replays all kept Gaussians over its 16 x 4 pixels ----
+#ifdef CVHRF_BWD_STATS
+      if (threadIdx.x == 0) atomicAdd(&g_bwd_stats[0], (unsigned long long)total);
+      if (lane == 0) atomicAdd(&g_bwd_stats[1], (unsigned long long)total);
+#endif
       for (int jj = 0; jj < total; ++jj) {
         const BwdG& gg = s_g[jj];
         const int q = s_pos[jj];
@@ -286,15 +304,14 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           if (lane < RL) s_part[warp][jj][lane] = 0.f;
           continue;
         }
+#ifdef CVHRF_BWD_STATS
+        if (lane == 0) atomicAdd(&g_bwd_stats[2], 1ull);
+#endif
         float v[kRedV];
         float4 cpx[C];
-        float2 cs[C];
 #pragma unroll
-        for (int c = 0; c < C; ++c) {
-          cpx[c] = s_cpx[c][jj];
-          cs[c] = s_cs[c][jj];
-        }
-        bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, cs, v);
+        for (int c = 0; c < C; ++c) cpx[c] = s_cpx[c][jj];
+        bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, v);
 #pragma unroll
         for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
         const float tot = warp_reduce_scatter16(v);
@@ -321,7 +338,19 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
                          : dcx * gg.B + dcz * gg.G;
         } else if (idx == 5) val = ww * S[0];
         else if (idx == 6) val = gg.opacity * S[0];
-        else val = s_part[0][j][idx - 1] + s_part[1][j][idx - 1] + s_part[2][j][idx - 1] + s_part[3][j][idx - 1];
+        else {
+          const int c = idx < 7 + C ? idx - 7 : idx - 7 - C;
+          const float X = s_part[0][j][6 + c] + s_part[1][j][6 + c] + s_part[2][j][6 + c] + s_part[3][j][6 + c];
+          const float Y = s_part[0][j][6 + C + c] + s_part[1][j][6 + C + c] + s_part[2][j][6 + C + c] +
+                          s_part[3][j][6 + C + c];
+          if (idx < 7 + C) {
+            const float2 cs = s_cs[c][j];
+            val = cs.x * X + cs.y * Y;
+          } else {
+            const float4 cp = s_cpx[c][j];
+            val = -cp.z * X + cp.x * Y;
+          }
+        }
         const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
         float* dst = records + (size_t)s_slot[j] * VR + ri;
           *dst += val;
@@ -391,6 +420,14 @@ __global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_
 }  // namespace cvhrf
 
 using namespace cvhrf;
+
+#ifdef CVHRF_BWD_STATS
+extern "C" void cvhrf_debug_bwd_stats(unsigned long long* out) {
+  cudaMemcpyFromSymbol(out, g_bwd_stats, sizeof(g_bwd_stats));
+  const unsigned long long z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  cudaMemcpyToSymbol(g_bwd_stats, z, sizeof(z));
+}
+#endif
 
 extern "C" size_t cvhrf_raster_backward_workspace_bytes(int num_pairs, int K, int C) {
   if (num_pairs < 0 || K < 1 || C < 1) return 0;
