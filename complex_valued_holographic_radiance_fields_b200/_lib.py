@@ -31,6 +31,13 @@ SIGNATURES = {
     "cvhrf_asm_propagate_planes_adjoint": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float_p,
                                                    c_float_p, c_float, c_float, c_void_p, c_void_p, c_size_t,
                                                    c_void_p]),
+    "cvhrf_asm_transfer_table_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "cvhrf_asm_transfer_table_build": (c_int, [c_void_p, c_int, c_int, c_float_p, c_float_p, c_float, c_float,
+                                               c_void_p, c_void_p]),
+    "cvhrf_asm_propagate_planes_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
+                                                 c_void_p, c_size_t, c_void_p]),
+    "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                                         c_void_p, c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_noalloc": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_float,
                                             c_float, c_float, c_float, c_int, c_void_p]),
     "cvhrf_raster_geometry_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

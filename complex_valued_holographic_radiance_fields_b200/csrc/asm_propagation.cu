@@ -497,6 +497,67 @@ __global__ void noalloc_tables_kernel(FftDesc d, float2* tw, float2* twP, int* d
 }  // namespace
 }  // namespace cvhrf
 
+// ---- precomputed transfer tables (compile-time sizes) ---------------------------------
+
+extern "C" size_t cvhrf_asm_transfer_table_bytes(int S, int K, int C) {
+  if (S < 1 || K < 1 || C < 1 || K * C > kMaxTableItems || !static_fft_size(S)) return 0;
+  return (size_t)K * C * 4 * S * S * sizeof(float2);
+}
+
+extern "C" int cvhrf_asm_transfer_table_build(const cvhrf_asm_plan* plan, int K, int C, const float* wavelengths,
+                                              const float* distances, float pixel_pitch, float aperture, void* table,
+                                              void* stream) {
+  if (!plan || !table || !wavelengths || !distances) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (K < 1 || C < 1 || K * C > kMaxTableItems) return CVHRF_EINVAL;
+  if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
+  TransferTable tt{};
+  for (int p = 0; p < K; ++p)
+    for (int c = 0; c < C; ++c) {
+      if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+      tt.tp[p * C + c] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, 2 * d.S);
+    }
+  return static_transfer_table(d, (float2*)table, tt, K * C, (cudaStream_t)stream);
+}
+
+extern "C" int cvhrf_asm_propagate_planes_table(const cvhrf_asm_plan* plan, const void* fields, int K, int C, int H,
+                                                int W, const void* table, void* holo, void* workspace,
+                                                size_t workspace_bytes, void* stream) {
+  if (!plan || !fields || !holo || !table) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (K < 1 || C < 1 || K * C > kMaxTableItems || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
+  if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
+  const int S = d.S, P = 2 * S;
+  Carver cv(workspace, workspace_bytes);
+  float2* A = cv.take<float2>((size_t)K * C * H * P);
+  float2* B = cv.take<float2>((size_t)C * S * P);
+  if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = static_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
+  if ((rc = static_columns_table(d, false, A, H, B, S, (const float2*)table, K, C, st))) return rc;
+  return static_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+}
+
+extern "C" int cvhrf_asm_propagate_planes_adjoint_table(const cvhrf_asm_plan* plan, const void* grad_holo, int K,
+                                                        int C, int H, int W, const void* table, void* grad_fields,
+                                                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (!plan || !grad_holo || !grad_fields || !table) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (K < 1 || C < 1 || K * C > kMaxTableItems || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
+  if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
+  const int S = d.S, P = 2 * S;
+  Carver cv(workspace, workspace_bytes);
+  float2* A = cv.take<float2>((size_t)C * S * P);
+  float2* B = cv.take<float2>((size_t)K * C * H * P);
+  if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
+  int rc;
+  if ((rc = static_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
+  if ((rc = static_columns_table(d, true, A, S, B, H, (const float2*)table, K, C, st))) return rc;
+  return static_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+}
+
 extern "C" int cvhrf_asm_propagate_noalloc(const void* in, int Hi, int Wi, void* out, int Ho, int Wo, int S,
                                            float wavelength, float pixel_pitch, float distance, float aperture,
                                            int accumulate, void* stream) {

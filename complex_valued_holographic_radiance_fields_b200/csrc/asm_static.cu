@@ -137,6 +137,125 @@ __global__ void __launch_bounds__(kThreads) rows_inverse_s(const float2* __restr
   }
 }
 
+// Transfer table of one input item: H[(q * 2 + h) * S + pos] = transfer x aperture at row
+// bin ku = 2 digrev[pos] + h and column bin kv of column q (the column pass layout).
+template <int S>
+__global__ void __launch_bounds__(kThreads) transfer_table_s(float2* __restrict__ table, const int* __restrict__ digrev,
+                                                            const TransferTable tt) {
+  constexpr int P = 2 * S;
+  const int item = blockIdx.y;
+  const TransferParams tp = tt.tp[item];
+  float2* H = table + (size_t)item * P * P;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < (size_t)P * P; e += (size_t)gridDim.x * blockDim.x) {
+    const int q = (int)(e / P), r = (int)(e - (size_t)q * P);
+    const int h = r / S, pos = r - h * S;
+    const int qh = q >= S ? 1 : 0;
+    const int kv = 2 * __ldg(&digrev[q - qh * S]) + qh;
+    const int ku = 2 * __ldg(&digrev[pos]) + h;
+    H[e] = transfer_at(ku, kv, P, tp);
+  }
+}
+
+// Column pass of a K-plane propagation with a precomputed transfer table: for channel c
+// = blockIdx.y, sum over planes p of H[p, c] * FFT(column of A[p * C + c]) is accumulated
+// in shared memory and inverse-transformed once (the inverse transform is linear), so a
+// column costs K forward transforms and one inverse.
+template <int S>
+__global__ void __launch_bounds__(kThreads) columns_sum_table_s(const float2* __restrict__ A, int Hi,
+                                                               float2* __restrict__ B, int Ho,
+                                                               const float2* __restrict__ tw,
+                                                               const float2* __restrict__ twP,
+                                                               const float2* __restrict__ table, int K, int C,
+                                                               int cols) {
+  extern __shared__ float2 sm[];
+  constexpr int P = 2 * S;
+  constexpr int LD = S + 1;
+  const int c = blockIdx.y;
+  const int q0 = blockIdx.x * cols;
+  const int ncols = min(cols, P - q0);
+  float2* spec = sm + 2 * cols * LD;
+  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
+  for (int p = 0; p < K; ++p) {
+    const float2* Ain = A + (size_t)(p * C + c) * Hi * P;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+      const int t = e / ncols, cc = e - t * ncols;
+      int pos = t;
+      int r = pos - oh;
+      if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
+      float2 v = make_float2(0.f, 0.f), vo = v;
+      if (r >= 0 && r < Hi) {
+        v = Ain[(size_t)r * P + q0 + cc];
+        vo = cmul(v, __ldg(&twP[pos]));
+      }
+      sm[(2 * cc) * LD + t] = v;
+      sm[(2 * cc + 1) * LD + t] = vo;
+    }
+    __syncthreads();
+    static_fft_forward_head<S>(sm, 2 * ncols, LD, tw);
+    static_last_forward_mul_acc<S>(sm, spec, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0, p == 0);
+    __syncthreads();
+  }
+  static_fft_inverse<S>(spec, 2 * ncols, LD, tw);
+  float2* Bout = B + (size_t)c * Ho * P;
+  for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+    const int rr = e / ncols, cc = e - rr * ncols;
+    const int n = oc + rr;
+    const int t = n >= S ? n - S : n;
+    Bout[(size_t)rr * P + q0 + cc] = cadd(spec[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), spec[(2 * cc + 1) * LD + t]));
+  }
+}
+
+// Adjoint column pass with the same table: the column of A[c] is transformed once, then
+// for every plane p the spectrum times conj(H[p, c]) (the transfer function of distance
+// -d_p) is inverse-transformed, cropped and written to B[p * C + c].
+template <int S>
+__global__ void __launch_bounds__(kThreads) columns_scatter_table_s(const float2* __restrict__ A, int Hi,
+                                                                   float2* __restrict__ B, int Ho,
+                                                                   const float2* __restrict__ tw,
+                                                                   const float2* __restrict__ twP,
+                                                                   const float2* __restrict__ table, int K, int C,
+                                                                   int cols) {
+  extern __shared__ float2 sm[];
+  constexpr int P = 2 * S;
+  constexpr int LD = S + 1;
+  const int c = blockIdx.y;
+  const int q0 = blockIdx.x * cols;
+  const int ncols = min(cols, P - q0);
+  float2* spec = sm + 2 * cols * LD;
+  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
+  const float2* Ain = A + (size_t)c * Hi * P;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+    const int t = e / ncols, cc = e - t * ncols;
+    int pos = t;
+    int r = pos - oh;
+    if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
+    float2 v = make_float2(0.f, 0.f), vo = v;
+    if (r >= 0 && r < Hi) {
+      v = Ain[(size_t)r * P + q0 + cc];
+      vo = cmul(v, __ldg(&twP[pos]));
+    }
+    spec[(2 * cc) * LD + t] = v;
+    spec[(2 * cc + 1) * LD + t] = vo;
+  }
+  __syncthreads();
+  static_fft_forward<S>(spec, 2 * ncols, LD, tw);
+  for (int p = 0; p < K; ++p) {
+    static_first_inverse_mul<S>(spec, sm, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0);
+    __syncthreads();
+    static_fft_inverse_rest<S>(sm, 2 * ncols, LD, tw);
+    float2* Bout = B + (size_t)(p * C + c) * Ho * P;
+    for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+      const int rr = e / ncols, cc = e - rr * ncols;
+      const int n = oc + rr;
+      const int t = n >= S ? n - S : n;
+      Bout[(size_t)rr * P + q0 + cc] = cadd(sm[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * cc + 1) * LD + t]));
+    }
+    __syncthreads();
+  }
+}
+
 constexpr size_t kStaticSmem = 64 * 1024;
 
 template <int S>
@@ -180,6 +299,33 @@ int run_rows_inverse(const float2* B, int total_rows, float2* out, int Wo, const
   const float P = 2.0f * S;
   rows_inverse_s<S><<<(total_rows + rows - 1) / rows, kThreads, smem, st>>>(B, total_rows, out, Wo, tw, twP, rows,
                                                                             1.0f / (P * P), accumulate);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+template <int S>
+int run_transfer_table(float2* table, const int* digrev, const TransferTable& tt, int items, cudaStream_t st) {
+  const size_t n = (size_t)4 * S * S;
+  const size_t nb = (n + kThreads - 1) / kThreads;
+  dim3 grid((unsigned)(nb < 1184 ? nb : 1184), items);
+  transfer_table_s<S><<<grid, kThreads, 0, st>>>(table, digrev, tt);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
+
+template <int S>
+int run_columns_table(bool adjoint, const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP,
+                      const float2* table, int K, int C, cudaStream_t st) {
+  const int cols = static_lines<S>(2 * (size_t)S * sizeof(float2) + 16, 104 * 1024);  // work + spectrum lines
+  const size_t smem = (size_t)cols * 4 * (S + 1) * sizeof(float2);
+  dim3 grid((2 * S + cols - 1) / cols, C);
+  if (!adjoint) {
+    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_sum_table_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    columns_sum_table_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C, cols);
+  } else {
+    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_scatter_table_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    columns_scatter_table_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C, cols);
+  }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
@@ -236,6 +382,33 @@ int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float
                         cudaStream_t st) {
 #define CALL run_rows_inverse
 #define ARGS (B, total_rows, out, Wo, d.tw, d.twP, accumulate, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+int static_transfer_table(const FftDesc& d, float2* table, const TransferTable& tt, int items, cudaStream_t st) {
+#define CALL run_transfer_table
+#define ARGS (table, d.digrev, tt, items, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+int static_columns_table(const FftDesc& d, bool adjoint, const float2* A, int Hi, float2* B, int Ho,
+                         const float2* table, int K, int C, cudaStream_t st) {
+#define CALL run_columns_table
+#define ARGS (adjoint, A, Hi, B, Ho, d.tw, d.twP, table, K, C, st)
   switch (d.S) {
     case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
     case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;

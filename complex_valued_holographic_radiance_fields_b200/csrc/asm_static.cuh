@@ -78,6 +78,12 @@ struct SumJobs {
   TransferParams tp[kMaxSumJobs][kMaxSumInputs];
 };
 
+// Transfer parameters of up to kMaxTableItems table items (item = p * C + c).
+constexpr int kMaxTableItems = 64;
+struct TransferTable {
+  TransferParams tp[kMaxTableItems];
+};
+
 // Sizes with a compile-time plan (the rest use the runtime plan of asm_propagation.cu).
 bool static_fft_size(int S);
 // Stage radices of the static plan (radix[0..2], *nst stages) for the digit-reversal table.
@@ -85,6 +91,12 @@ void static_fft_radices(int S, int* radix, int* nst);
 int static_rows_forward(const FftDesc& d, const float2* in, int total_rows, int Wi, float2* A, cudaStream_t st);
 int static_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho, const SumJobs& jobs, int njobs,
                    cudaStream_t st);
+// Precomputed transfer tables (items x P x P complex64, column-pass layout).
+int static_transfer_table(const FftDesc& d, float2* table, const TransferTable& tt, int items, cudaStream_t st);
+// Column pass with a table: adjoint = false sums K planes per channel (A: K*C items,
+// B: C items); adjoint = true scatters each channel to K planes (A: C items, B: K*C).
+int static_columns_table(const FftDesc& d, bool adjoint, const float2* A, int Hi, float2* B, int Ho,
+                         const float2* table, int K, int C, cudaStream_t st);
 int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float2* out, int Wo, int accumulate,
                         cudaStream_t st);
 

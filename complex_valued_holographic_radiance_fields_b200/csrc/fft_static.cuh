@@ -226,4 +226,88 @@ __device__ __forceinline__ void static_fft_inverse(float2* sm, int nlines, int l
   __syncthreads();
 }
 
+// The last forward stage (its L is 1) fused with a pointwise spectrum product: instead of
+// writing the stage's outputs back, x * H is stored (first) or added into `spec` at the
+// same positions.  H holds, per line pair (column q = q0 + line / 2, half h = line % 2),
+// S values in position order: H[((q0 + line / 2) * 2 + h) * S + pos].
+template <int S>
+__device__ __forceinline__ void static_last_forward_mul_acc(float2* sm, float2* spec, int nlines, int ld,
+                                                            const float2* __restrict__ H, int q0, bool first) {
+  using P = StaticPlan<S>;
+  constexpr int ST = P::nst - 1;
+  constexpr int R = P::R(ST), L = P::L(ST);
+  static_assert(L == 1, "last stage has unit stride");
+  constexpr int bpl = S / R;
+  const int total = nlines * bpl;
+  for (int b = threadIdx.x; b < total; b += blockDim.x) {
+    const int line = b / bpl;
+    const int blk = b - line * bpl;
+    const int off = line * ld + blk * R;
+    const float2* hp = H + ((size_t)(q0 + (line >> 1)) * 2 + (line & 1)) * S + blk * R;
+    float2 x[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) x[m] = sm[off + m];
+    regdft<R>(x);
+#pragma unroll
+    for (int m = 0; m < R; ++m) {
+      const float2 y = cmul(x[m], __ldg(&hp[m]));
+      spec[off + m] = first ? y : cadd(spec[off + m], y);
+    }
+  }
+}
+
+// The first inverse stage fused with a pointwise product by conj(H) (same H layout as
+// above): reads `spec`, writes the stage's outputs to `sm`; the remaining inverse stages
+// then run on `sm` (static_fft_inverse_rest).
+template <int S>
+__device__ __forceinline__ void static_first_inverse_mul(const float2* spec, float2* sm, int nlines, int ld,
+                                                         const float2* __restrict__ H, int q0) {
+  using P = StaticPlan<S>;
+  constexpr int ST = P::nst - 1;
+  constexpr int R = P::R(ST), L = P::L(ST);
+  static_assert(L == 1, "last stage has unit stride");
+  constexpr int bpl = S / R;
+  const int total = nlines * bpl;
+  for (int b = threadIdx.x; b < total; b += blockDim.x) {
+    const int line = b / bpl;
+    const int blk = b - line * bpl;
+    const int off = line * ld + blk * R;
+    const float2* hp = H + ((size_t)(q0 + (line >> 1)) * 2 + (line & 1)) * S + blk * R;
+    float2 x[R];
+#pragma unroll
+    for (int m = 0; m < R; ++m) x[m] = cconj(cmul(spec[off + m], cconj(__ldg(&hp[m]))));
+    regdft<R>(x);
+#pragma unroll
+    for (int m = 0; m < R; ++m) sm[off + m] = cconj(x[m]);
+  }
+}
+
+// Forward transform without its last stage (used with static_last_forward_mul_acc).
+template <int S>
+__device__ __forceinline__ void static_fft_forward_head(float2* sm, int nlines, int ld, const float2* tw) {
+  using P = StaticPlan<S>;
+  if constexpr (P::nst > 1) {
+    static_stage<S, 0, false>(sm, nlines, ld, tw);
+    __syncthreads();
+  }
+  if constexpr (P::nst > 2) {
+    static_stage<S, 1, false>(sm, nlines, ld, tw);
+    __syncthreads();
+  }
+}
+
+// Inverse transform without its first stage (used after static_first_inverse_mul).
+template <int S>
+__device__ __forceinline__ void static_fft_inverse_rest(float2* sm, int nlines, int ld, const float2* tw) {
+  using P = StaticPlan<S>;
+  if constexpr (P::nst > 2) {
+    static_stage<S, 1, true>(sm, nlines, ld, tw);
+    __syncthreads();
+  }
+  if constexpr (P::nst > 1) {
+    static_stage<S, 0, true>(sm, nlines, ld, tw);
+    __syncthreads();
+  }
+}
+
 }  // namespace cvhrf

@@ -117,6 +117,32 @@ def BandlimitedPropagation(field, wavelength, pixel_pitch, distance, size, use_c
     return BandlimitedPropagationFunction.apply(field, wavelength, pixel_pitch, distance, size, aperture_size)
 
 
+_tables = {}
+_tables_lock = threading.Lock()
+
+
+def transfer_table(S, K, C, wavelengths, distances, pixel_pitch, aperture_size, device):
+    """The precomputed transfer tables of a (K planes x C wavelengths) propagation
+    (cvhrf_asm_transfer_table_build), cached per configuration; None where the size has
+    no compile-time plan.  Built on first use (make that first call outside stream capture)."""
+    L = _lib.lib()
+    nbytes = L.cvhrf_asm_transfer_table_bytes(int(S), int(K), int(C))
+    if nbytes == 0:
+        return None
+    key = (torch.device(device), int(S), tuple(wavelengths), tuple(distances), float(pixel_pitch), float(aperture_size))
+    with _tables_lock:
+        t = _tables.get(key)
+        if t is None:
+            t = torch.empty(nbytes, dtype=torch.uint8, device=device)
+            _lib.check(L.cvhrf_asm_transfer_table_build(get_plan(S, device), int(K), int(C),
+                                                        _lib.float_array(wavelengths), _lib.float_array(distances),
+                                                        float(pixel_pitch), float(aperture_size),
+                                                        ctypes.c_void_p(t.data_ptr()), _stream(t)),
+                       "cvhrf_asm_transfer_table_build")
+            _tables[key] = t
+    return t
+
+
 class PlanePropagationFunction(torch.autograd.Function):
     """Fused plane/channel loop of model.py:1251-1272.
 
@@ -126,7 +152,7 @@ class PlanePropagationFunction(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0):
+    def forward(ctx, fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0, use_table=True):
         fields = _check_field(fields, "fields")
         K, C, H, W = fields.shape
         wl = [_scalar(w) for w in wavelengths]
@@ -137,6 +163,16 @@ class PlanePropagationFunction(torch.autograd.Function):
         holo = torch.empty((C, S, S), dtype=torch.complex64, device=fields.device)
         ws = _workspace(S, K * C, H, C, S, fields.device)
         L = _lib.lib()
+        table = transfer_table(S, K, C, wl, ds, ctx.cfg[2], ctx.cfg[4], fields.device) if use_table else None
+        ctx.table = table
+        if table is not None:
+            with timed("propagation_forward"):
+                st = L.cvhrf_asm_propagate_planes_table(get_plan(S, fields.device), ctypes.c_void_p(fields.data_ptr()),
+                                                        K, C, H, W, ctypes.c_void_p(table.data_ptr()),
+                                                        ctypes.c_void_p(holo.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                        ws.numel(), _stream(fields))
+            _lib.check(st, "cvhrf_asm_propagate_planes_table")
+            return holo
         with timed("propagation_forward"):
             st = L.cvhrf_asm_propagate_planes(get_plan(S, fields.device), ctypes.c_void_p(fields.data_ptr()), K, C, H,
                                           W, _lib.float_array(wl), _lib.float_array(ds), ctx.cfg[2], ctx.cfg[4],
@@ -152,14 +188,24 @@ class PlanePropagationFunction(torch.autograd.Function):
         grad_fields = torch.empty((K, C, H, W), dtype=torch.complex64, device=g.device)
         ws = _workspace(S, C, S, K * C, H, g.device)
         L = _lib.lib()
+        if ctx.table is not None:
+            with timed("propagation_backward"):
+                st = L.cvhrf_asm_propagate_planes_adjoint_table(get_plan(S, g.device), ctypes.c_void_p(g.data_ptr()), K,
+                                                                C, H, W, ctypes.c_void_p(ctx.table.data_ptr()),
+                                                                ctypes.c_void_p(grad_fields.data_ptr()),
+                                                                ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(g))
+            _lib.check(st, "cvhrf_asm_propagate_planes_adjoint_table")
+            return grad_fields, None, None, None, None, None, None
         with timed("propagation_backward"):
             st = L.cvhrf_asm_propagate_planes_adjoint(get_plan(S, g.device), ctypes.c_void_p(g.data_ptr()), K, C, H, W,
                                                   _lib.float_array(wl), _lib.float_array(ds), pitch, ap,
                                                   ctypes.c_void_p(grad_fields.data_ptr()),
                                                   ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(g))
         _lib.check(st, "cvhrf_asm_propagate_planes_adjoint")
-        return grad_fields, None, None, None, None, None
+        return grad_fields, None, None, None, None, None, None
 
 
-def propagate_planes(fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0):
-    return PlanePropagationFunction.apply(fields, wavelengths, distances, pixel_pitch, S, aperture_size)
+def propagate_planes(fields, wavelengths, distances, pixel_pitch, S, aperture_size=-1.0, use_table=True):
+    """Sum over planes of the propagated fields.  `use_table` reads the transfer
+    function from a cached precomputed table (transfer_table) where the size allows."""
+    return PlanePropagationFunction.apply(fields, wavelengths, distances, pixel_pitch, S, aperture_size, use_table)

@@ -108,6 +108,36 @@ int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan,
                                        void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Precomputed transfer tables for cvhrf_asm_propagate_planes and its adjoint.
+ * The transfer function x aperture of every (plane p, channel c) depends only on
+ * (S, wavelength, distance, pitch, aperture), which stay fixed across a training
+ * run, so it can be evaluated once (same values as the per-call evaluation) and
+ * read back by the column pass.  A table holds K*C items of (2S)^2 complex64 values
+ * in the column pass's order (item p*C + c); only sizes with a compile-time FFT
+ * plan (S = 64, 128, 256, 384, 512, 800, 1024, 1920, 2048) are supported, and
+ * K*C <= 64.  cvhrf_asm_transfer_table_bytes returns 0 for unsupported arguments.
+ * The table-based calls take the same fields / holo / workspace as
+ * cvhrf_asm_propagate_planes(_adjoint); with a table the column pass makes K
+ * forward and one inverse column transform per channel (the spectra of the K
+ * planes are summed before the inverse transform), and the adjoint one forward and
+ * K inverse ones (it uses conj(H), the transfer function of distance -d).
+ * No counterpart in the reference, whose BandlimitedPropagation evaluates the
+ * transfer function in every call (bandlimited_propagation_cuda.cu:29-86).
+ */
+size_t cvhrf_asm_transfer_table_bytes(int S, int K, int C);
+int cvhrf_asm_transfer_table_build(const cvhrf_asm_plan* plan, int K, int C,
+                                   const float* wavelengths, const float* distances,
+                                   float pixel_pitch, float aperture, void* table, void* stream);
+int cvhrf_asm_propagate_planes_table(const cvhrf_asm_plan* plan,
+                                     const void* fields, int K, int C, int H, int W,
+                                     const void* table, void* holo,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_asm_propagate_planes_adjoint_table(const cvhrf_asm_plan* plan,
+                                             const void* grad_holo, int K, int C, int H, int W,
+                                             const void* table, void* grad_fields,
+                                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * cvhrf_asm_propagate without any device allocation and without a plan.
  * No counterpart in the reference: it exists for callers that cannot allocate
  * device memory when they propagate (a frozen or exhausted memory pool, a plugin

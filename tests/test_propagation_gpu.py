@@ -96,3 +96,26 @@ def test_planes_vs_per_call(cuda):
     exp_g = torch.stack([torch.stack([P.propagate(g[c], wl[c], 8e-6, -ds[p], S, float(S), out_hw=(H, W))
                                       for c in range(C)]) for p in range(K)])
     assert rel(fr.grad, exp_g) < TOL
+
+
+@pytest.mark.parametrize("S,H,W,K,C", [(64, 48, 64, 2, 1), (128, 100, 128, 3, 3), (256, 256, 200, 1, 2),
+                                       (800, 800, 800, 3, 3)])
+@pytest.mark.parametrize("ap", [-1.0, None])
+def test_planes_table_matches_per_call_transfer(cuda, S, H, W, K, C, ap):
+    """Precomputed transfer table (K forward + 1 inverse column transforms per channel)
+    against the per-call evaluation (one forward + inverse per plane), forward and adjoint."""
+    from complex_valued_holographic_radiance_fields_b200 import propagation as P
+    ap = float(S) if ap is None else ap
+    fields = torch.stack([torch.stack([rand_field(H, W, 7 * p + c) for c in range(C)]) for p in range(K)]).to(cuda)
+    wl = [639e-9, 532e-9, 473e-9][:C]
+    ds = [4e-3, 2e-3, 0.0][:K]
+    g = torch.stack([rand_field(S, S, 90 + c) for c in range(C)]).to(cuda)
+    out = []
+    for use_table in (True, False):
+        fr = fields.clone().requires_grad_(True)
+        holo = P.propagate_planes(fr, wl, ds, 8e-6, S, ap, use_table=use_table)
+        holo.backward(g)
+        out.append((holo.detach(), fr.grad))
+    assert P.transfer_table(S, K, C, wl, ds, 8e-6, ap, cuda) is not None
+    assert rel(out[0][0], out[1][0]) < 1e-5
+    assert rel(out[0][1], out[1][1]) < 1e-5
