@@ -24,19 +24,24 @@ __global__ void __launch_bounds__(kThreads) rows_forward_s(const float2* __restr
   const int row0 = blockIdx.x * rows;
   const int nrows = min(rows, total_rows - row0);
   if (nrows <= 0) return;
+  // all of the block's row loads in flight at once (asynchronous copies), then the odd
+  // half-lines are formed in place
   for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
     const int r = e / S, t = e - r * S;
-    const float2* src = in + (size_t)(row0 + r) * Wi;
-    int pos = t;
-    int j = pos - ow;
-    if (j < 0 || j >= Wi) { pos = t + S; j = pos - ow; }
-    float2 v = make_float2(0.f, 0.f), vo = v;
-    if (j >= 0 && j < Wi) {
-      v = src[j];
-      vo = cmul(v, __ldg(&twP[pos]));
-    }
-    sm[(2 * r) * S + t] = v;
-    sm[(2 * r + 1) * S + t] = vo;
+    int j = t - ow;
+    if (j < 0 || j >= Wi) j = t + S - ow;
+    float2* dst = sm + (2 * r) * S + t;
+    if (j >= 0 && j < Wi) cp_async8(dst, in + (size_t)(row0 + r) * Wi + j);
+    else *dst = make_float2(0.f, 0.f);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+  for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
+    const int r = e / S, t = e - r * S;
+    const int j = t - ow;
+    const int pos = (j < 0 || j >= Wi) ? t + S : t;
+    sm[(2 * r + 1) * S + t] = cmul(sm[(2 * r) * S + t], __ldg(&twP[pos]));
   }
   __syncthreads();
   static_fft_forward<S>(sm, 2 * nrows, S, tw);
@@ -119,8 +124,10 @@ __global__ void __launch_bounds__(kThreads) rows_inverse_s(const float2* __restr
   if (nrows <= 0) return;
   for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
     const int r = e / P, q = e - r * P;
-    sm[(2 * r) * S + q] = B[(size_t)(row0 + r) * P + q];
+    cp_async8(sm + (2 * r) * S + q, B + (size_t)(row0 + r) * P + q);
   }
+  cp_async_commit();
+  cp_async_wait_all();
   __syncthreads();
   static_fft_inverse<S>(sm, 2 * nrows, S, tw);
   const int oc = (P - Wo) / 2;
@@ -159,46 +166,58 @@ __global__ void __launch_bounds__(kThreads) transfer_table_s(float2* __restrict_
 // Column pass of a K-plane propagation with a precomputed transfer table: for channel c
 // = blockIdx.y, sum over planes p of H[p, c] * FFT(column of A[p * C + c]) is accumulated
 // in shared memory and inverse-transformed once (the inverse transform is linear), so a
-// column costs K forward transforms and one inverse.
-template <int S>
-__global__ void __launch_bounds__(kThreads) columns_sum_table_s(const float2* __restrict__ A, int Hi,
-                                                               float2* __restrict__ B, int Ho,
-                                                               const float2* __restrict__ tw,
-                                                               const float2* __restrict__ twP,
-                                                               const float2* __restrict__ table, int K, int C,
-                                                               int cols) {
+// column costs K forward transforms and one inverse.  The columns of plane p + 1 are
+// fetched with asynchronous copies into a staging line while plane p is transformed.
+// Shared memory: 2 COLS work lines, 2 COLS spectrum lines, COLS staging lines (stride S+1).
+template <int S, int COLS, int NT>
+__global__ void __launch_bounds__(NT) columns_sum_table_s(const float2* __restrict__ A, int Hi,
+                                                         float2* __restrict__ B, int Ho,
+                                                         const float2* __restrict__ tw,
+                                                         const float2* __restrict__ twP,
+                                                         const float2* __restrict__ table, int K, int C) {
   extern __shared__ float2 sm[];
   constexpr int P = 2 * S;
   constexpr int LD = S + 1;
+  float2* work = sm;
+  float2* spec = sm + 2 * COLS * LD;
+  float2* raw = sm + 4 * COLS * LD;
   const int c = blockIdx.y;
-  const int q0 = blockIdx.x * cols;
-  const int ncols = min(cols, P - q0);
-  float2* spec = sm + 2 * cols * LD;
+  const int q0 = blockIdx.x * COLS;
+  const int ncols = min(COLS, P - q0);
   const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
-  for (int p = 0; p < K; ++p) {
-    const float2* Ain = A + (size_t)(p * C + c) * Hi * P;
-#pragma unroll 4
-    for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+  auto fetch = [&](int p) {
+    const float2* Ain = A + (size_t)(p * C + c) * Hi * P + q0;
+    for (int e = threadIdx.x; e < ncols * S; e += NT) {
       const int t = e / ncols, cc = e - t * ncols;
-      int pos = t;
-      int r = pos - oh;
-      if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
-      float2 v = make_float2(0.f, 0.f), vo = v;
-      if (r >= 0 && r < Hi) {
-        v = Ain[(size_t)r * P + q0 + cc];
-        vo = cmul(v, __ldg(&twP[pos]));
-      }
-      sm[(2 * cc) * LD + t] = v;
-      sm[(2 * cc + 1) * LD + t] = vo;
+      int r = t - oh;
+      if (r < 0 || r >= Hi) r = t + S - oh;
+      float2* dst = raw + cc * LD + t;
+      if (r >= 0 && r < Hi) cp_async8(dst, Ain + (size_t)r * P + cc);
+      else *dst = make_float2(0.f, 0.f);
+    }
+    cp_async_commit();
+  };
+  fetch(0);
+  for (int p = 0; p < K; ++p) {
+    cp_async_wait_all();
+    __syncthreads();
+    for (int e = threadIdx.x; e < ncols * S; e += NT) {
+      const int cc = e / S, t = e - cc * S;
+      const int r = t - oh;
+      const int pos = (r < 0 || r >= Hi) ? t + S : t;
+      const float2 v = raw[cc * LD + t];
+      work[(2 * cc) * LD + t] = v;
+      work[(2 * cc + 1) * LD + t] = cmul(v, __ldg(&twP[pos]));
     }
     __syncthreads();
-    static_fft_forward_head<S>(sm, 2 * ncols, LD, tw);
-    static_last_forward_mul_acc<S>(sm, spec, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0, p == 0);
-    __syncthreads();
+    if (p + 1 < K) fetch(p + 1);
+    static_fft_forward_head<S>(work, 2 * ncols, LD, tw);
+    static_last_forward_mul_acc<S>(work, spec, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0, p == 0);
   }
+  __syncthreads();
   static_fft_inverse<S>(spec, 2 * ncols, LD, tw);
   float2* Bout = B + (size_t)c * Ho * P;
-  for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+  for (int e = threadIdx.x; e < Ho * ncols; e += NT) {
     const int rr = e / ncols, cc = e - rr * ncols;
     const int n = oc + rr;
     const int t = n >= S ? n - S : n;
@@ -209,48 +228,52 @@ __global__ void __launch_bounds__(kThreads) columns_sum_table_s(const float2* __
 // Adjoint column pass with the same table: the column of A[c] is transformed once, then
 // for every plane p the spectrum times conj(H[p, c]) (the transfer function of distance
 // -d_p) is inverse-transformed, cropped and written to B[p * C + c].
-template <int S>
-__global__ void __launch_bounds__(kThreads) columns_scatter_table_s(const float2* __restrict__ A, int Hi,
-                                                                   float2* __restrict__ B, int Ho,
-                                                                   const float2* __restrict__ tw,
-                                                                   const float2* __restrict__ twP,
-                                                                   const float2* __restrict__ table, int K, int C,
-                                                                   int cols) {
+// Shared memory: 2 COLS spectrum lines and 2 COLS work lines (stride S+1).
+template <int S, int COLS, int NT>
+__global__ void __launch_bounds__(NT) columns_scatter_table_s(const float2* __restrict__ A, int Hi,
+                                                             float2* __restrict__ B, int Ho,
+                                                             const float2* __restrict__ tw,
+                                                             const float2* __restrict__ twP,
+                                                             const float2* __restrict__ table, int K, int C) {
   extern __shared__ float2 sm[];
   constexpr int P = 2 * S;
   constexpr int LD = S + 1;
+  float2* work = sm;
+  float2* spec = sm + 2 * COLS * LD;
   const int c = blockIdx.y;
-  const int q0 = blockIdx.x * cols;
-  const int ncols = min(cols, P - q0);
-  float2* spec = sm + 2 * cols * LD;
+  const int q0 = blockIdx.x * COLS;
+  const int ncols = min(COLS, P - q0);
   const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
-  const float2* Ain = A + (size_t)c * Hi * P;
-#pragma unroll 4
-  for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
+  const float2* Ain = A + (size_t)c * Hi * P + q0;
+  for (int e = threadIdx.x; e < ncols * S; e += NT) {
     const int t = e / ncols, cc = e - t * ncols;
-    int pos = t;
-    int r = pos - oh;
-    if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
-    float2 v = make_float2(0.f, 0.f), vo = v;
-    if (r >= 0 && r < Hi) {
-      v = Ain[(size_t)r * P + q0 + cc];
-      vo = cmul(v, __ldg(&twP[pos]));
-    }
-    spec[(2 * cc) * LD + t] = v;
-    spec[(2 * cc + 1) * LD + t] = vo;
+    int r = t - oh;
+    if (r < 0 || r >= Hi) r = t + S - oh;
+    float2* dst = spec + (2 * cc) * LD + t;
+    if (r >= 0 && r < Hi) cp_async8(dst, Ain + (size_t)r * P + cc);
+    else *dst = make_float2(0.f, 0.f);
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncthreads();
+  for (int e = threadIdx.x; e < ncols * S; e += NT) {
+    const int cc = e / S, t = e - cc * S;
+    const int r = t - oh;
+    const int pos = (r < 0 || r >= Hi) ? t + S : t;
+    spec[(2 * cc + 1) * LD + t] = cmul(spec[(2 * cc) * LD + t], __ldg(&twP[pos]));
   }
   __syncthreads();
   static_fft_forward<S>(spec, 2 * ncols, LD, tw);
   for (int p = 0; p < K; ++p) {
-    static_first_inverse_mul<S>(spec, sm, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0);
+    static_first_inverse_mul<S>(spec, work, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0);
     __syncthreads();
-    static_fft_inverse_rest<S>(sm, 2 * ncols, LD, tw);
+    static_fft_inverse_rest<S>(work, 2 * ncols, LD, tw);
     float2* Bout = B + (size_t)(p * C + c) * Ho * P;
-    for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
+    for (int e = threadIdx.x; e < Ho * ncols; e += NT) {
       const int rr = e / ncols, cc = e - rr * ncols;
       const int n = oc + rr;
       const int t = n >= S ? n - S : n;
-      Bout[(size_t)rr * P + q0 + cc] = cadd(sm[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * cc + 1) * LD + t]));
+      Bout[(size_t)rr * P + q0 + cc] = cadd(work[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), work[(2 * cc + 1) * LD + t]));
     }
     __syncthreads();
   }
@@ -313,18 +336,22 @@ int run_transfer_table(float2* table, const int* digrev, const TransferTable& tt
   return CVHRF_OK;
 }
 
+
 template <int S>
 int run_columns_table(bool adjoint, const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP,
                       const float2* table, int K, int C, cudaStream_t st) {
-  const int cols = static_lines<S>(2 * (size_t)S * sizeof(float2) + 16, 104 * 1024);  // work + spectrum lines
-  const size_t smem = (size_t)cols * 4 * (S + 1) * sizeof(float2);
-  dim3 grid((2 * S + cols - 1) / cols, C);
+  constexpr int COLS = S >= 1024 ? 1 : 3, NT = 256;  // 3 columns: 77 KB for S = 800, two CTAs per SM
+  dim3 grid((2 * S + COLS - 1) / COLS, C);
   if (!adjoint) {
-    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_sum_table_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    columns_sum_table_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C, cols);
+    const size_t smem = (size_t)COLS * 5 * (S + 1) * sizeof(float2);
+    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_sum_table_s<S, COLS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)smem));
+    columns_sum_table_s<S, COLS, NT><<<grid, NT, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C);
   } else {
-    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_scatter_table_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    columns_scatter_table_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C, cols);
+    const size_t smem = (size_t)COLS * 4 * (S + 1) * sizeof(float2);
+    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_scatter_table_s<S, COLS, NT>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    columns_scatter_table_s<S, COLS, NT><<<grid, NT, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C);
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
