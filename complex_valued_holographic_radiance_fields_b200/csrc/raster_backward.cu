@@ -161,7 +161,8 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float 
   r[5] = gdyy.x + gdyy.y;
 }
 
-// One CTA per 16x16 tile, 128 threads x 2 horizontally adjacent pixels, one pass per
+// One CTA per 16x16 tile, 128 threads x 2 horizontally adjacent pixels (each warp an 8 x 8
+// quadrant, which keeps the per-warp footprint test tight), one pass per
 // plane.  Each pass stages the tile list back to front in batches, keeps only the
 // Gaussians that can contribute on this plane inside this tile (plane weight >= 1e-6,
 // alpha >= 1/255 box meets the tile, position below the tile's largest n_contrib), and
@@ -190,7 +191,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   const int tile = blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int px = tx * kTile + (threadIdx.x & 7) * 2, py = ty * kTile + (threadIdx.x >> 3);
+  const int px = tx * kTile + (warp & 1) * 8 + (lane & 3) * 2, py = ty * kTile + (warp >> 1) * 8 + (lane >> 2);
   const bool in0 = px < W && py < H, in1 = px + 1 < W && py < H;
   const float2 npx = make_float2(-(float)px, -(float)(px + 1));
   const float pyf = (float)py;
@@ -287,7 +288,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         }
       }
       __syncthreads();
-      // ---- each warp replays all kept Gaussians over its 16 x 4 pixels ----
+      // ---- each warp replays all kept Gaussians over its 8 x 8 pixels ----
 #ifdef CVHRF_BWD_STATS
       if (threadIdx.x == 0) atomicAdd(&g_bwd_stats[0], (unsigned long long)total);
       if (lane == 0) atomicAdd(&g_bwd_stats[1], (unsigned long long)total);
