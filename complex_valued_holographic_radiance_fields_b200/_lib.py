@@ -38,6 +38,10 @@ SIGNATURES = {
                                                  c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                                          c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_intensity_loss_workspace_bytes": (c_size_t, [c_int]),
+    "cvhrf_intensity_loss_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "cvhrf_intensity_loss": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_intensity_loss_backward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "cvhrf_asm_propagate_noalloc": (c_int, [c_void_p, c_int, c_int, c_void_p, c_int, c_int, c_int, c_float,
                                             c_float, c_float, c_float, c_int, c_void_p]),
     "cvhrf_raster_geometry_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

@@ -227,7 +227,11 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
       }
       __syncthreads();
       const int cnt = c0 + c1 + c2 + c3;
+      // a warp whose 128 pixels have all stopped skips the batch (it only adds exact zeros)
+      if (__all_sync(0xffffffffu, mine_done)) continue;
       for (int jj = 0; jj < cnt; ++jj) {
+        if ((jj & 31) == 31 && __all_sync(0xffffffffu, TA.x < 1e-4f && TA.y < 1e-4f && TB.x < 1e-4f && TB.y < 1e-4f))
+          break;
         const float4 mo = s_mo[jj];
         const float4 k0 = s_c0[jj], k1 = s_c1[jj];
         const float2 mx = make_float2(mo.x, mo.y);

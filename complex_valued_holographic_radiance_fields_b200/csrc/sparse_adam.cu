@@ -14,6 +14,17 @@ namespace cvhrf {
 namespace {
 
 constexpr int kMaxGroups = 16;
+// One element of the update, in the reference's operation order (moments first, then
+// p += -lr m / (sqrt(v) + eps)).
+__device__ __forceinline__ void adam_element(const cvhrf_adam_group& G, size_t idx, float b1, float b2) {
+  const float g = G.grad[idx];
+  const float m = b1 * G.exp_avg[idx] + (1.0f - b1) * g;
+  const float v = b2 * G.exp_avg_sq[idx] + (1.0f - b2) * g * g;
+  G.param[idx] += -G.lr * m / (sqrtf(v) + G.eps);
+  G.exp_avg[idx] = m;
+  G.exp_avg_sq[idx] = v;
+}
+
 struct AdamLaunch {
   int n;
   cvhrf_adam_group g[kMaxGroups];
@@ -33,15 +44,7 @@ __global__ void __launch_bounds__(256) sparse_adam_kernel(AdamLaunch L, const in
   const int d = (int)(local - r * G.D);
   const long long row = G.dense ? r : visible[r];
   const size_t idx = (size_t)row * G.D + d;
-  const float Register_param_grad = G.grad[idx];
-  float Register_exp_avg = G.exp_avg[idx];
-  float Register_exp_avg_sq = G.exp_avg_sq[idx];
-  Register_exp_avg = b1 * Register_exp_avg + (1.0f - b1) * Register_param_grad;
-  Register_exp_avg_sq = b2 * Register_exp_avg_sq + (1.0f - b2) * Register_param_grad * Register_param_grad;
-  const float step = -G.lr * Register_exp_avg / (sqrtf(Register_exp_avg_sq) + G.eps);
-  G.param[idx] += step;
-  G.exp_avg[idx] = Register_exp_avg;
-  G.exp_avg_sq[idx] = Register_exp_avg_sq;
+  adam_element(G, idx, b1, b2);
 }
 
 }  // namespace
@@ -92,15 +95,7 @@ __global__ void __launch_bounds__(256) sparse_adam_masked_kernel(AdamLaunch L, c
   const long long row = local / G.D;
   if (!G.dense && (row >= mask_len || mask[row] == 0)) return;
   const size_t idx = (size_t)local;
-  const float Register_param_grad = G.grad[idx];
-  float Register_exp_avg = G.exp_avg[idx];
-  float Register_exp_avg_sq = G.exp_avg_sq[idx];
-  Register_exp_avg = b1 * Register_exp_avg + (1.0f - b1) * Register_param_grad;
-  Register_exp_avg_sq = b2 * Register_exp_avg_sq + (1.0f - b2) * Register_param_grad * Register_param_grad;
-  const float step = -G.lr * Register_exp_avg / (sqrtf(Register_exp_avg_sq) + G.eps);
-  G.param[idx] += step;
-  G.exp_avg[idx] = Register_exp_avg;
-  G.exp_avg_sq[idx] = Register_exp_avg_sq;
+  adam_element(G, idx, b1, b2);
 }
 
 __global__ void rows_to_mask_kernel(const int64_t* __restrict__ rows, int V, int mask_len, uint8_t* mask) {

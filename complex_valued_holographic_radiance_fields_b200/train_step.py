@@ -2,7 +2,7 @@
 
     render (model.py:1365-1416)   -> splat_tile_cuda           (libcvhrf rasterizer)
     per-plane propagation + sum   -> propagate_planes          (libcvhrf fused FFT/ASM)
-    loss = mean((|holo|^2 - target)^2)                          (torch, elementwise)
+    loss = mean((|holo|^2 - target)^2)   -> intensity_l2_loss         (libcvhrf, 2 launches)
     backward                      -> libcvhrf adjoints
     SparseGaussianAdam.step(visible)                            (libcvhrf fused Adam)
 
@@ -25,6 +25,7 @@ sort permutation (``idxs[visible]``) so the update lands on the rows that were s
 import torch
 
 from . import scene as SC
+from .loss import intensity_l2_loss
 from .optimizer import SparseGaussianAdam
 from .propagation import propagate_planes
 from . import rasterizer as RZ
@@ -64,7 +65,7 @@ class HoloTrainer:
         field, visible = splat_tile_cuda(*SC.splat_args(kw))
         holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
         tgt = self.target if target is None else target
-        loss = ((holo.real.square() + holo.imag.square() - tgt) ** 2).mean()
+        loss = intensity_l2_loss(holo, tgt)
         return loss, idxs[visible]
 
     def step(self, target=None):
@@ -80,7 +81,7 @@ class HoloTrainer:
         kw, idxs = SC.render_inputs_fused(self.params, self.camera)
         field, vis_mask = SplatTileCudaCapacity.apply(*SC.splat_args(kw), self.pairs_capacity)
         holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
-        loss = ((holo.real.square() + holo.imag.square() - target) ** 2).mean()
+        loss = intensity_l2_loss(holo, target)
         n = self.params["means"].shape[0]
         row_mask = torch.zeros(n, dtype=torch.uint8, device=self.device)
         row_mask.scatter_(0, idxs, vis_mask)

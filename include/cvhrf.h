@@ -305,6 +305,26 @@ int cvhrf_scene_backward(const cvhrf_gaussians* gaussians, const float* R, const
                          float* d_colours, float* d_pre_phase, float* d_pre_opacities, float* d_pre_planes,
                          void* stream);
 
+/* ---- L2 intensity loss of the training iteration --------------------------- */
+/*
+ * loss = mean_i ((|holo_i|^2 - target_i)^2) over n complex64 holo values and n float
+ * targets (train.py computes this with torch elementwise ops).  One launch; *loss is
+ * a DEVICE float.  The workspace (cvhrf_intensity_loss_workspace_bytes) holds block
+ * partials and a completion counter: zero it once with
+ * cvhrf_intensity_loss_init_workspace; each call leaves it ready for the next (also
+ * when replayed from a captured graph).  Calls sharing a workspace must be ordered on
+ * one stream.  holo must be 16-byte and target 8-byte aligned.  The partial sums are
+ * combined in a fixed order, so the result is deterministic.
+ * Backward: grad_holo = (*grad_loss / n) * 2 r * 2 holo, r = |holo|^2 - target, with
+ * *grad_loss a DEVICE float (the upstream gradient).
+ */
+size_t cvhrf_intensity_loss_workspace_bytes(int n);
+int cvhrf_intensity_loss_init_workspace(void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_intensity_loss(const void* holo, const float* target, int n, float* loss,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_intensity_loss_backward(const void* holo, const float* target, int n, const float* grad_loss,
+                                  void* grad_holo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
