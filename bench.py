@@ -200,10 +200,12 @@ def run_mine(args, world, rank, local):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        if graph:
-            float(tr.replay(host_tgt).item())     # pinned host target -> static device buffer inside
-        else:
+    if graph:
+        # every step: host->device copy of its target (pipelined on a side stream) and a
+        # device->host read of its loss, through the trainer's public entry point
+        tr.train_from_host([host_tgt] * args.steps)
+    else:
+        for _ in range(args.steps):
             dev_tgt.copy_(host_tgt, non_blocking=True)
             float(step(dev_tgt).item())
     e1.record()

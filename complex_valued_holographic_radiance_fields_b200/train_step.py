@@ -129,6 +129,39 @@ class HoloTrainer:
         self.graph.replay()
         return self._static_loss
 
+    def train_from_host(self, host_targets):
+        """One captured iteration per target in `host_targets` (CPU tensors, ideally pinned),
+        returning each iteration's loss as a host float (read after the iteration).  The
+        next target's host->device copy runs on a side stream while the current iteration
+        computes; the iteration itself starts with a device-to-device copy of its target
+        into the graph's input buffer."""
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        side = getattr(self, "_copy_stream", None)
+        if side is None:
+            side = self._copy_stream = torch.cuda.Stream(dev)
+            self._staging = torch.empty_like(self._static_target)
+        ready, consumed = torch.cuda.Event(), torch.cuda.Event()
+        targets = list(host_targets)
+        losses = []
+        side.wait_stream(main)
+        if targets:
+            with torch.cuda.stream(side):
+                self._staging.copy_(targets[0], non_blocking=True)
+                ready.record(side)
+        for i in range(len(targets)):
+            main.wait_event(ready)
+            self._static_target.copy_(self._staging, non_blocking=True)
+            consumed.record(main)
+            if i + 1 < len(targets):
+                with torch.cuda.stream(side):
+                    side.wait_event(consumed)
+                    self._staging.copy_(targets[i + 1], non_blocking=True)
+                    ready.record(side)
+            self.graph.replay()
+            losses.append(float(self._static_loss.item()))
+        return losses
+
     def graph_overflowed(self):
         """True if any replay since capture exceeded the pair capacity (synchronises)."""
         return bool(self._overflow_acc.item())

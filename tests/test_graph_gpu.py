@@ -84,3 +84,17 @@ def test_graph_replay_with_new_target(cuda):
     lb = b.replay(tgt)
     torch.cuda.synchronize()
     assert torch.equal(la, lb)
+
+
+def test_train_from_host_matches_eager(cuda):
+    a, b = _trainer(cuda), _trainer(cuda)
+    b.capture(headroom=1.5, warmup=2)
+    for _ in range(3):
+        a.step()
+    g = torch.Generator().manual_seed(9)
+    targets = [torch.rand(a.target.shape, generator=g).pin_memory() for _ in range(4)]
+    la = [a.step(t.to(cuda)).item() for t in targets]
+    lb = b.train_from_host(targets)
+    assert la == lb
+    for k in a.params:
+        assert torch.equal(a.params[k], b.params[k]), k
