@@ -300,6 +300,56 @@ def ref_cuda_step_rate(steps, warmup):
             "what": "reference CUDA kernels (cov3d_cuda + cuda_modules, rebuilt sm_100a) + cuFFT, same step"}
 
 
+METRIC5 = "train iters/sec (fwd+bwd+sparse Adam) @1M Gaussians, 1008x756, K=7, planes sharded over GPUs"
+CONFIG5 = {"workload": "config5: full training step, 1M Gaussians in a depth-[1,10] frustum, 1008x756, K=7 planes, "
+                       "3 wavelengths, 2x-padded ASM propagation (2048^2) at 8 um, L2 intensity loss, sparse Adam",
+           "gaussians": 1000000, "image": [1008, 756], "planes": 7, "pad": 2048,
+           "l2_policy": "inputs larger than L2"}
+
+
+def run_config5(args, world, rank, local):
+    """Plane-parallel config 5 (strong scaling: one training iteration split over the GPUs by plane)."""
+    import math
+    from complex_valued_holographic_radiance_fields_b200 import _lib, scene as SC
+    from complex_valued_holographic_radiance_fields_b200.train_step import PlaneShardedTrainer
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    W, H = 1008, 756
+    cam = SC.PinholeCamera(W, H)
+    ht = math.tan(cam.fov / 2.0)
+    tr = PlaneShardedTrainer(N=1000000, W=W, H=H, K=7, S=1024, device=dev, camera=cam, rank=rank, world=world,
+                             frustum=(1.0, 10.0, ht, ht * H / W, -5.0, 0.7, 4.0))
+    for _ in range(args.warmup):
+        tr.step()
+    L = _lib.lib()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    l0 = L.cvhrf_kernel_launch_count()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        loss = tr.step()
+    t1.record()
+    barrier()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank != 0:
+        return None
+    return {"metric": METRIC5, "value": 1000.0 / ms, "unit": "iters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded, config-5 shapes)",
+            "config": dict(CONFIG5, parallelism=f"plane-shard{world}", planes_on_rank0=tr.planes),
+            "execution": "eager", "gpu_launches": int(L.cvhrf_kernel_launch_count() - l0),
+            "loss": float(loss.item())}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -324,6 +374,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config3", choices=["config3", "config5"],
+                    help="config3 (default, the BASELINE metric) or config5 (plane-parallel, strong scaling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -333,6 +385,8 @@ def main():
     try:
         if args.impl == "reference":
             line = run_reference(args, world, rank)
+        elif args.workload == "config5":
+            line = run_config5(args, world, rank, local)
         else:
             line = run_mine(args, world, rank, local)
             if line is not None and world == 1 and not args.no_cpu_baseline:

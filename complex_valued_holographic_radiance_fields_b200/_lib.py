@@ -57,6 +57,8 @@ SIGNATURES = {
     "cvhrf_scene_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_scene_prepare": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_float, c_void_p, c_size_t]
                             + [c_void_p] * 9 + [c_void_p]),
+    "cvhrf_scene_prepare_owned": (c_int, [c_void_p, c_void_p, c_void_p, c_float, c_float, ctypes.c_uint32, c_void_p,
+                                          c_size_t] + [c_void_p] * 9 + [c_void_p]),
     "cvhrf_scene_backward": (c_int, [c_void_p, c_void_p, c_void_p] + [c_void_p] * 14 + [c_void_p]),
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_sparse_adam_masked": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),

@@ -10,6 +10,12 @@
 //             dlog s = ds * s, normalize backward, mod passes through, sigmoid', and
 //             the straight-through softmax(x / 0.001) * g (model.py:51-56).
 //
+// Plane ownership (cvhrf_scene_prepare_owned, for plane-parallel training): rows whose
+// one-hot plane is not in the owned set are treated like rows outside (near, far): sorted
+// last, and given depth z = near so that the rasterizer culls them.  With
+// one-hot plane weights that is exact for the owned planes: such a row has weight 0 on
+// every owned plane, so it neither renders there nor receives gradient there.
+//
 // Rows outside (near, far) are not dropped: they are sorted after every valid row (key
 // 0xFFFFFFFF) and keep their out-of-range depth, so the rasterizer culls them (radius 0,
 // no tiles, not visible) and their gradients come back as exact zeros.  This removes the
@@ -31,14 +37,24 @@ __device__ __forceinline__ uint32_t float_order_key(float z) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-__global__ void glue_keys_kernel(int N, const float* __restrict__ means, const float* __restrict__ R,
-                                 const float* __restrict__ T, float near_plane, float far_plane,
+// index of the largest plane logit, first one on ties (the one-hot of glue_gather_kernel)
+__device__ __forceinline__ int argmax_plane(const float* logits, int K) {
+  int best = 0;
+  float bv = logits[0];
+  for (int k = 1; k < K; ++k)
+    if (logits[k] > bv) { bv = logits[k]; best = k; }
+  return best;
+}
+
+__global__ void glue_keys_kernel(cvhrf_gaussians G, const float* __restrict__ R, const float* __restrict__ T,
+                                 float near_plane, float far_plane, uint32_t owned_planes,
                                  uint32_t* __restrict__ keys, uint32_t* __restrict__ vals) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= N) return;
+  if (r >= G.N) return;
   float c[3];
-  cam_point(means + 3 * r, R, T, c);
-  const bool valid = c[2] > near_plane && c[2] < far_plane;
+  cam_point(G.means + 3 * r, R, T, c);
+  bool valid = c[2] > near_plane && c[2] < far_plane;
+  if (owned_planes != 0xFFFFFFFFu) valid = valid && ((owned_planes >> argmax_plane(G.pre_planes + r * G.K, G.K)) & 1u);
   uint32_t k = valid ? float_order_key(c[2]) : 0xFFFFFFFFu;
   if (valid && k == 0xFFFFFFFFu) k = 0xFFFFFFFEu;
   keys[r] = k;
@@ -46,13 +62,17 @@ __global__ void glue_keys_kernel(int N, const float* __restrict__ means, const f
 }
 
 __global__ void glue_gather_kernel(cvhrf_gaussians G, const float* __restrict__ R, const float* __restrict__ T,
-                                   const uint32_t* __restrict__ order, float* cam, float* z, float* quats,
-                                   float* scales, float* colours, float* phase, float* opac, float* planes) {
+                                   const uint32_t* __restrict__ order, uint32_t owned_planes, float cull_z,
+                                   float* cam, float* z, float* quats, float* scales, float* colours, float* phase,
+                                   float* opac, float* planes) {
   const int s = blockIdx.x * blockDim.x + threadIdx.x;
   if (s >= G.N) return;
   const int r = (int)order[s];
   float c[3];
   cam_point(G.means + 3 * r, R, T, c);
+  const int best = argmax_plane(G.pre_planes + r * G.K, G.K);
+  // a row of a plane this caller does not own is culled through its depth (z = near)
+  if (owned_planes != 0xFFFFFFFFu && !((owned_planes >> best) & 1u)) c[2] = cull_z;
 #pragma unroll
   for (int j = 0; j < 3; ++j) cam[3 * s + j] = c[j];
   z[s] = c[2];
@@ -70,12 +90,6 @@ __global__ void glue_gather_kernel(cvhrf_gaussians G, const float* __restrict__ 
     phase[s * G.C + k] = m;
   }
   opac[s] = 1.0f / (1.0f + expf(-G.pre_opac[r]));
-  int best = 0;
-  float bv = G.pre_planes[r * G.K];
-  for (int k = 1; k < G.K; ++k) {
-    const float v = G.pre_planes[r * G.K + k];
-    if (v > bv) { bv = v; best = k; }
-  }
   for (int k = 0; k < G.K; ++k) planes[s * G.K + k] = k == best ? 1.0f : 0.0f;
 }
 
@@ -139,10 +153,11 @@ extern "C" size_t cvhrf_scene_workspace_bytes(int N) {
   return 4 * align_up(n * sizeof(uint32_t), 256) + align_up(sort_scratch_words((int)n) * sizeof(uint32_t), 256);
 }
 
-extern "C" int cvhrf_scene_prepare(const cvhrf_gaussians* G, const float* R, const float* T, float near_plane,
-                                   float far_plane, void* ws, size_t ws_bytes, int32_t* order, float* cam_means,
-                                   float* z_vals, float* quats, float* scales, float* colours, float* phase,
-                                   float* opacities, float* plane_probs, void* stream) {
+extern "C" int cvhrf_scene_prepare_owned(const cvhrf_gaussians* G, const float* R, const float* T,
+                                         float near_plane, float far_plane, uint32_t owned_planes, void* ws,
+                                         size_t ws_bytes, int32_t* order, float* cam_means, float* z_vals,
+                                         float* quats, float* scales, float* colours, float* phase,
+                                         float* opacities, float* plane_probs, void* stream) {
   if (!gaussians_ok(G) || !R || !T) return CVHRF_EINVAL;
   const int N = G->N;
   if (N == 0) return CVHRF_OK;
@@ -157,16 +172,24 @@ extern "C" int cvhrf_scene_prepare(const cvhrf_gaussians* G, const float* R, con
   if (cv.overflow || !ws) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   const int nb = (N + 255) / 256;
-  glue_keys_kernel<<<nb, 256, 0, st>>>(N, G->means, R, T, near_plane, far_plane, k0, v0);
+  glue_keys_kernel<<<nb, 256, 0, st>>>(*G, R, T, near_plane, far_plane, owned_planes, k0, v0);
   CVHRF_LAUNCH_CHECK();
   int alt = 0, rc;
   if ((rc = radix_sort_pairs(k0, v0, k1, v1, N, 0, 32, scr, st, &alt))) return rc;
   const uint32_t* ord = alt ? v1 : v0;
   CVHRF_CUDA_TRY(cudaMemcpyAsync(order, ord, N * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
-  glue_gather_kernel<<<nb, 256, 0, st>>>(*G, R, T, ord, cam_means, z_vals, quats, scales, colours, phase, opacities,
-                                         plane_probs);
+  glue_gather_kernel<<<nb, 256, 0, st>>>(*G, R, T, ord, owned_planes, near_plane, cam_means, z_vals, quats, scales,
+                                         colours, phase, opacities, plane_probs);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
+}
+
+extern "C" int cvhrf_scene_prepare(const cvhrf_gaussians* G, const float* R, const float* T, float near_plane,
+                                   float far_plane, void* ws, size_t ws_bytes, int32_t* order, float* cam_means,
+                                   float* z_vals, float* quats, float* scales, float* colours, float* phase,
+                                   float* opacities, float* plane_probs, void* stream) {
+  return cvhrf_scene_prepare_owned(G, R, T, near_plane, far_plane, 0xFFFFFFFFu, ws, ws_bytes, order, cam_means,
+                                   z_vals, quats, scales, colours, phase, opacities, plane_probs, stream);
 }
 
 extern "C" int cvhrf_scene_backward(const cvhrf_gaussians* G, const float* R, const int32_t* order,

@@ -47,6 +47,62 @@ def _shared_flat_buffer(params):
     return flat if total == flat.numel() else None
 
 
+class _AllReduceSum(torch.autograd.Function):
+    """Sum of a tensor over the ranks; its gradient is the incoming gradient itself (the
+    summed tensor feeds an identical computation on every rank, so every rank receives
+    the same upstream gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        y = x.contiguous().clone()
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+def all_reduce_sum(x, group=None):
+    """Differentiable all-reduce (sum) across the process group."""
+    return _AllReduceSum.apply(x, group)
+
+
+def exchange_and_step(trainer, visible, group=None):
+    """Sum the gradients and union the visible rows across ranks, then step the optimizer.
+    Ranks that produced no gradients (nothing rendered) contribute zeros."""
+    from . import _lib
+    import ctypes
+    n = trainer.params["means"].shape[0]
+    dev = trainer.params["means"].device
+    if any(p.grad is None for p in trainer.params.values()):
+        total = sum(p.numel() for p in trainer.params.values())
+        flat = torch.zeros(total, dtype=torch.float32, device=dev)
+        off = 0
+        for p in trainer.params.values():
+            if p.grad is None:
+                p.grad = flat[off:off + p.numel()].view_as(p)
+            else:
+                flat[off:off + p.numel()].copy_(p.grad.reshape(-1))
+                p.grad = flat[off:off + p.numel()].view_as(p)
+            off += p.numel()
+    else:
+        flat = _shared_flat_buffer(trainer.params)
+        if flat is None:
+            rows = allreduce_gradients_and_visibility(trainer.params, visible, n, group)
+            trainer.opt.step(rows)
+            return
+    mask = torch.empty(n, dtype=torch.uint8, device=dev)
+    vis = visible.to(torch.int64).contiguous()
+    _lib.check(_lib.lib().cvhrf_rows_to_mask(ctypes.c_void_p(vis.data_ptr()), vis.numel(),
+                                             ctypes.c_void_p(mask.data_ptr()), n,
+                                             ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)),
+               "cvhrf_rows_to_mask")
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=group)
+    trainer.opt.step(row_mask=mask)
+
+
 def dp_step(trainer, target=None, group=None):
     """One view-parallel training iteration on `trainer` (a HoloTrainer).
 

@@ -174,7 +174,7 @@ class FusedRenderInputs(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, means, pq, ps, col, pph, pop, ppl, R, T, near, far):
+    def forward(ctx, means, pq, ps, col, pph, pop, ppl, R, T, near, far, owned_planes=0xFFFFFFFF):
         import ctypes
         from . import _lib
         dev = means.device
@@ -190,9 +190,10 @@ class FusedRenderInputs(torch.autograd.Function):
         outs = [torch.empty(N, 3, **f32), torch.empty(N, **f32), torch.empty(N, 4, **f32), torch.empty(N, 3, **f32),
                 torch.empty(N, C, **f32), torch.empty(N, C, **f32), torch.empty(N, **f32), torch.empty(N, K, **f32)]
         st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        _lib.check(L.cvhrf_scene_prepare(ctypes.byref(G), R.data_ptr(), T.data_ptr(), float(near), float(far),
-                                         ws.data_ptr(), ws.numel(), order.data_ptr(),
-                                         *[o.data_ptr() for o in outs], st), "cvhrf_scene_prepare")
+        _lib.check(L.cvhrf_scene_prepare_owned(ctypes.byref(G), R.data_ptr(), T.data_ptr(), float(near), float(far),
+                                               int(owned_planes) & 0xFFFFFFFF, ws.data_ptr(), ws.numel(),
+                                               order.data_ptr(), *[o.data_ptr() for o in outs], st),
+                   "cvhrf_scene_prepare_owned")
         ctx.save_for_backward(*ins, R, order)
         ctx.mark_non_differentiable(order, outs[1])
         return (*outs, order)
@@ -222,13 +223,15 @@ class FusedRenderInputs(torch.autograd.Function):
         _lib.check(_lib.lib().cvhrf_scene_backward(ctypes.byref(G), R.data_ptr(), order.data_ptr(),
                                                      *[t.data_ptr() for t in gs], *[t.data_ptr() for t in d], st),
                    "cvhrf_scene_backward")
-        return (*d, None, None, None, None)
+        return (*d, None, None, None, None, None)
 
 
-def render_inputs_fused(params, camera):
-    """Same contract as `render_inputs`, through the fused kernels (all rows, culled by depth)."""
+def render_inputs_fused(params, camera, owned_planes=0xFFFFFFFF):
+    """Same contract as `render_inputs`, through the fused kernels (all rows, culled by depth).
+    `owned_planes` (bit p = plane p) additionally culls the rows whose one-hot plane is not
+    owned (plane-parallel training)."""
     R, T = camera.on(params["means"].device)
-    outs = FusedRenderInputs.apply(*[params[k] for k in _PARAM_ORDER], R, T, camera.near, camera.far)
+    outs = FusedRenderInputs.apply(*[params[k] for k in _PARAM_ORDER], R, T, camera.near, camera.far, owned_planes)
     cam, z, q, s, col, ph, op, pl, order = outs
     kw = dict(cam_means_3D=cam, z_vals=z, quats=q, scales=s, colours=col, phase=ph, opacities=op, plane_probs=pl,
               fx=camera.fx, fy=camera.fy, px=camera.px, py=camera.py,

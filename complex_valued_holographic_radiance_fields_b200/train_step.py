@@ -42,10 +42,10 @@ def plane_distances(K, volume_depth=4e-3, d_val=-2e-3):
 
 class HoloTrainer:
     def __init__(self, N=300000, W=800, H=800, K=3, pitch=8e-6, lr=1e-3, eps=1e-15, seed=0, device="cuda",
-                 camera=None, wavelengths=None, target=None):
+                 camera=None, wavelengths=None, target=None, S=None, frustum=None):
         self.device = torch.device(device)
         self.W, self.H, self.K = W, H, K
-        self.S = max(W, H)
+        self.S = S or max(W, H)   # pad size (train.py: max(W, H) unless configured)
         self.aperture = float(self.S)
         self.pitch = pitch
         self.wavelengths = list(wavelengths or WAVELENGTHS)
@@ -53,17 +53,36 @@ class HoloTrainer:
         self.prop_distances = [float(-d[p]) for p in range(K)]
         self.camera = camera or SC.PinholeCamera(W, H)
         self.params = {k: v.requires_grad_(True) for k, v in
-                       SC.make_gaussians(N, K=K, C=len(self.wavelengths), seed=seed, device=self.device).items()}
+                       SC.make_gaussians(N, K=K, C=len(self.wavelengths), seed=seed, device=self.device,
+                                         frustum=frustum).items()}
         self.opt = SparseGaussianAdam([{"params": [p], "lr": lr} for p in self.params.values()], lr=lr, eps=eps)
         if target is None:
             g = torch.Generator().manual_seed(1)
             target = torch.rand(len(self.wavelengths), self.S, self.S, generator=g)
         self.target = target.to(self.device)
 
+    # The planes this trainer renders: all of them here; a plane-parallel trainer
+    # (PlaneShardedTrainer) renders its share and sums the holograms across GPUs.
+    planes = None
+    owned_mask = 0xFFFFFFFF
+
+    def _render_inputs(self):
+        kw, idxs = SC.render_inputs_fused(self.params, self.camera, self.owned_mask)
+        if self.planes is not None:
+            kw["plane_probs"] = kw["plane_probs"].index_select(1, self._plane_idx)
+        return kw, idxs
+
+    def _hologram(self, field):
+        ds = self.prop_distances if self.planes is None else [self.prop_distances[p] for p in self.planes]
+        return self._combine(propagate_planes(field, self.wavelengths, ds, self.pitch, self.S, self.aperture))
+
+    def _combine(self, holo):
+        return holo
+
     def forward(self, target=None):
-        kw, idxs = SC.render_inputs_fused(self.params, self.camera)
+        kw, idxs = self._render_inputs()
         field, visible = splat_tile_cuda(*SC.splat_args(kw))
-        holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
+        holo = self._hologram(field)
         tgt = self.target if target is None else target
         loss = intensity_l2_loss(holo, tgt)
         return loss, idxs[visible]
@@ -78,9 +97,9 @@ class HoloTrainer:
 
     # ---- CUDA-graph mode ------------------------------------------------------------
     def _forward_capacity(self, target):
-        kw, idxs = SC.render_inputs_fused(self.params, self.camera)
+        kw, idxs = self._render_inputs()
         field, vis_mask = SplatTileCudaCapacity.apply(*SC.splat_args(kw), self.pairs_capacity)
-        holo = propagate_planes(field, self.wavelengths, self.prop_distances, self.pitch, self.S, self.aperture)
+        holo = self._hologram(field)
         loss = intensity_l2_loss(holo, target)
         n = self.params["means"].shape[0]
         row_mask = torch.zeros(n, dtype=torch.uint8, device=self.device)
@@ -165,3 +184,50 @@ class HoloTrainer:
     def graph_overflowed(self):
         """True if any replay since capture exceeded the pair capacity (synchronises)."""
         return bool(self._overflow_acc.item())
+
+
+class PlaneShardedTrainer(HoloTrainer):
+    """Plane-parallel training (one process per GPU): GPU r renders, propagates and
+    back-propagates only the planes it owns (p % world == rank) and the Gaussians whose
+    one-hot plane is one of them; the per-channel holograms are summed across GPUs with
+    one all-reduce before the loss (whose gradient is then the same on every GPU), and
+    the Gaussian gradients (disjoint between GPUs: each Gaussian lives on one plane) and
+    the visibility masks are combined before the identical sparse Adam step.  With one
+    process it is the plain trainer.  A GPU that owns no plane (world > K) contributes
+    zeros.  Parameters must be identical on every rank (same seed)."""
+
+    def __init__(self, *args, rank=0, world=1, group=None, **kw):
+        super().__init__(*args, **kw)
+        self.rank, self.world, self.group = rank, world, group
+        self.planes = [p for p in range(self.K) if p % world == rank]
+        self.owned_mask = sum(1 << p for p in self.planes)
+        self._plane_idx = torch.tensor(self.planes, dtype=torch.long, device=self.device)
+
+    def _combine(self, holo):
+        import torch.distributed as dist
+        if self.world == 1 or not dist.is_initialized():
+            return holo
+        from .distributed import all_reduce_sum
+        return all_reduce_sum(holo, self.group)
+
+    def forward(self, target=None):
+        if self.planes:
+            return super().forward(target)
+        from .distributed import all_reduce_sum
+        C = len(self.wavelengths)
+        holo = all_reduce_sum(torch.zeros((C, self.S, self.S), dtype=torch.complex64, device=self.device), self.group)
+        loss = intensity_l2_loss(holo, self.target if target is None else target)
+        return loss, torch.empty(0, dtype=torch.long, device=self.device)
+
+    def step(self, target=None):
+        from .distributed import exchange_and_step
+        for p in self.params.values():
+            p.grad = None
+        loss, visible = self.forward(target)
+        loss.backward()
+        import torch.distributed as dist
+        if self.world > 1 and dist.is_initialized():
+            exchange_and_step(self, visible, self.group)
+        else:
+            self.opt.step(visible)
+        return loss.detach()

@@ -297,6 +297,16 @@ int cvhrf_scene_prepare(const cvhrf_gaussians* gaussians, const float* R, const 
                         float far_plane, void* workspace, size_t workspace_bytes, int32_t* order,
                         float* cam_means, float* z_vals, float* quats, float* scales, float* colours,
                         float* phase, float* opacities, float* plane_probs, void* stream);
+/*
+ * cvhrf_scene_prepare restricted to a set of planes (bit p of owned_planes = plane p,
+ * K <= 32; 0xFFFFFFFF = all): rows whose one-hot plane is not owned are sorted last and
+ * culled like rows outside (near, far).  Used by plane-parallel training, where each GPU
+ * renders only the planes it owns.  No counterpart in the reference.
+ */
+int cvhrf_scene_prepare_owned(const cvhrf_gaussians* gaussians, const float* R, const float* T, float near_plane,
+                              float far_plane, uint32_t owned_planes, void* workspace, size_t workspace_bytes,
+                              int32_t* order, float* cam_means, float* z_vals, float* quats, float* scales,
+                              float* colours, float* phase, float* opacities, float* plane_probs, void* stream);
 /* Backward of cvhrf_scene_prepare: gradients of the sorted rows -> parameter rows (every row written). */
 int cvhrf_scene_backward(const cvhrf_gaussians* gaussians, const float* R, const int32_t* order,
                          const float* g_cam_means, const float* g_quats, const float* g_scales,

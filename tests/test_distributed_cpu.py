@@ -44,3 +44,40 @@ def test_allreduce_two_ranks():
         assert a == [[3.0] * 3] * 6
         assert b == [float(3 * i) for i in range(6)]
         assert u == [0, 2, 4]
+
+
+def _worker_allreduce_sum(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from complex_valued_holographic_radiance_fields_b200.distributed import all_reduce_sum
+    x = torch.full((4,), float(rank + 1), requires_grad=True)
+    y = all_reduce_sum(x * 2.0)
+    w = torch.arange(4, dtype=torch.float32)
+    (y * w).sum().backward()
+    q.put((rank, y.tolist(), x.grad.tolist()))
+    dist.destroy_process_group()
+
+
+def test_all_reduce_sum_autograd_two_ranks():
+    """The plane-parallel hologram sum: forward sums over ranks, backward passes the
+    (replicated) upstream gradient through unchanged."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker_allreduce_sum, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, y, g in res:
+        assert y == [6.0] * 4
+        assert g == [0.0, 2.0, 4.0, 6.0]
+
+
+def test_plane_ownership():
+    from complex_valued_holographic_radiance_fields_b200.train_step import PlaneShardedTrainer
+    owned = [[p for p in range(7) if p % 8 == r] for r in range(8)]
+    assert owned[7] == [] and sorted(sum(owned, [])) == list(range(7))
+    assert PlaneShardedTrainer.__mro__[1].__name__ == "HoloTrainer"
