@@ -38,6 +38,11 @@ SIGNATURES = {
                                                  c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                                          c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_sort_pairs_workspace_bytes": (c_size_t, [c_int]),
+    "cvhrf_sort_pairs_u32": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_inclusive_scan_workspace_bytes": (c_size_t, [c_int]),
+    "cvhrf_inclusive_scan_u32": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_lookback_timeouts": (c_int, []),
     "cvhrf_intensity_loss_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_intensity_loss_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
     "cvhrf_intensity_loss": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

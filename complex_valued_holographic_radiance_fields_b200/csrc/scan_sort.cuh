@@ -1,4 +1,5 @@
-// Device-wide inclusive scan and stable LSD radix sort (u32 keys, u32 values).
+// Device-wide inclusive scan and stable LSD radix sort (u32 keys, u32 values), both
+// single-pass with decoupled look-back (one launch per scan, one per sort pass).
 //
 // These replace the CUB calls of the reference binning (cub::DeviceScan::InclusiveSum,
 // rasterizer_splat.cu:427, and cub::DeviceRadixSort::SortPairs, :475-480).  The sort
@@ -40,5 +41,8 @@ int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int
 //  n is then the capacity the launch grids are sized for.)
 // *flag = 1 if keys[0..n) is non-decreasing, else 0 (device int, stream-ordered).
 int keys_sorted_flag(const uint32_t* keys, int n, int* flag, cudaStream_t st);
+// Number of look-back waits that ran out of their iteration limit since the library was
+// loaded (each makes that scan/sort result invalid; expected 0).  Synchronises.
+int lookback_timeouts();
 
 }  // namespace cvhrf

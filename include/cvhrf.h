@@ -315,6 +315,25 @@ int cvhrf_scene_backward(const cvhrf_gaussians* gaussians, const float* R, const
                          float* d_colours, float* d_pre_phase, float* d_pre_opacities, float* d_pre_planes,
                          void* stream);
 
+/* ---- binning primitives ----------------------------------------------------- */
+/*
+ * The scan and the stable radix sort the rasterizer's binning uses, as standalone calls
+ * (replace cub::DeviceScan::InclusiveSum, rasterizer_splat.cu:427, and
+ * cub::DeviceRadixSort::SortPairs, :475-480).  Both are single-pass with decoupled
+ * look-back: one launch per scan, one histogram launch plus one launch per 8-bit pass
+ * per sort.  The sort orders (keys, values) in place by key bits [begin_bit, end_bit),
+ * stably; n < 2^30.
+ * cvhrf_lookback_timeouts: how many look-back waits ran out of their iteration limit
+ * since the library was loaded (each invalidates that result; expected 0; synchronises).
+ */
+size_t cvhrf_sort_pairs_workspace_bytes(int n);
+int cvhrf_sort_pairs_u32(uint32_t* keys, uint32_t* values, int n, int begin_bit, int end_bit,
+                         void* workspace, size_t workspace_bytes, void* stream);
+size_t cvhrf_inclusive_scan_workspace_bytes(int n);
+int cvhrf_inclusive_scan_u32(const uint32_t* in, uint32_t* out, int n, void* workspace,
+                             size_t workspace_bytes, void* stream);
+int cvhrf_lookback_timeouts(void);
+
 /* ---- L2 intensity loss of the training iteration --------------------------- */
 /*
  * loss = mean_i ((|holo_i|^2 - target_i)^2) over n complex64 holo values and n float
