@@ -2,7 +2,7 @@
 // elementwise ops: loss = mean((|holo|^2 - target)^2) over C x S x S).
 //
 // Forward: one launch; blocks reduce grid-stride partial sums of r^2 (r = re^2 + im^2 -
-// target) and the last block to finish sums the partials in block order (deterministic)
+// target) and the last block to finish sums the partials in a fixed order (deterministic)
 // and writes loss = sum / n.  Backward: one elementwise launch,
 //   dL/dholo = (g / n) * 2 r * 2 (re, im)     (g = upstream gradient, a device scalar)
 // in torch's convention for complex inputs (d/dre + i d/dim).
@@ -48,12 +48,17 @@ __global__ void __launch_bounds__(kLossThreads) intensity_loss_kernel(const floa
     last = atomicAdd(done, 1u) == gridDim.x - 1;
   }
   __syncthreads();
-  if (last && threadIdx.x == 0) {
+  if (last && threadIdx.x < 32) {
+    // the last block: lane l sums partials l, l + 32, ... in order, then a fixed shuffle tree
     __threadfence();
     double total = 0.0;
-    for (int b = 0; b < (int)gridDim.x; ++b) total += (double)((volatile float*)partials)[b];
-    *loss = (float)(total / (double)n);
-    *done = 0u;  // ready for the next launch (also inside a replayed graph)
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += 32) total += (double)((volatile float*)partials)[b];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+    if (threadIdx.x == 0) {
+      *loss = (float)(total / (double)n);
+      *done = 0u;  // ready for the next launch (also inside a replayed graph)
+    }
   }
 }
 

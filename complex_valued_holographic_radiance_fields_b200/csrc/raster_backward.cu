@@ -112,16 +112,17 @@ constexpr int red_len() { return 6 + 2 * C; }
 // A pixel that does not contribute (masked, power > 0, alpha < 1/255) gets alpha = 0 and
 // gd = 0, which leaves its state unchanged exactly (T / 1, 0 P + 1 Q) and adds exact zeros.
 template <int C>
-__device__ __forceinline__ void bwd_pair(PairState<C>& st, const BwdG& g, float w, float2 dx, float dy, bool n0,
+__device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, float w, float2 dx, float dy, bool n0,
                                          bool n1, const float4* cpx, float* r) {
+  // con = (conic_x, conic_y, conic_z, opacity)
   const float2 dy2 = make_float2(dy, dy);
-  const float2 cx2 = make_float2(g.cx, g.cx);
-  const float czdd = g.cz * dy * dy;
-  const float ncydy = -(g.cy * dy);
+  const float2 cx2 = make_float2(con.x, con.x);
+  const float czdd = con.z * dy * dy;
+  const float ncydy = -(con.y * dy);
   const float2 quad = __ffma2_rn(__fmul2_rn(cx2, dx), dx, make_float2(czdd, czdd));
   const float2 power = __ffma2_rn(make_float2(-0.5f, -0.5f), quad, __fmul2_rn(make_float2(ncydy, ncydy), dx));
   const float2 G = make_float2(expf(power.x), expf(power.y));
-  const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(g.opacity, g.opacity), G), make_float2(w, w));
+  const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(con.w, con.w), G), make_float2(w, w));
   const float al0 = fminf(0.99f, aw.x), al1 = fminf(0.99f, aw.y);
   const bool a0 = n0 && power.x <= 0.0f && al0 >= 1.0f / 255.0f;
   const bool a1 = n1 && power.y <= 0.0f && al1 >= 1.0f / 255.0f;
@@ -178,9 +179,11 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL + 1;
   static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
-  __shared__ int s_pos[NB];
-  __shared__ BwdG s_g[NB];
-  __shared__ float s_w[NB];
+  __shared__ float4 s_geo[NB];      // (mean x, mean y, box half-width, box half-height): the footprint test
+  __shared__ float2 s_wq[NB];       // (plane weight, list position as int bits)
+  __shared__ float4 s_con[NB];      // (conic x, conic y, conic z, opacity): the pixel arithmetic
+  __shared__ float4 s_coefA[NB];    // (A, B, Cc, D) and
+  __shared__ float2 s_coefB[NB];    // (E, G): d cov / d conic, used once per (tile, Gaussian)
   __shared__ float4 s_cpx[C][NB];   // (re, re, im, im) of colour * e^{i phase}
   __shared__ float2 s_cs[C][NB];    // (cos, sin)
   __shared__ float s_part[NW][NB][RP];
@@ -275,9 +278,11 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
       if (keep) {
         const int idx = off + __popc(bal & lt);
         s_slot[idx] = slot_sorted[range.x + pos];
-        s_pos[idx] = pos;
-        s_g[idx] = g;
-        s_w[idx] = w;
+        s_geo[idx] = make_float4(g.mx, g.my, g.ex, g.ey);
+        s_wq[idx] = make_float2(w, __int_as_float(pos));
+        s_con[idx] = make_float4(g.cx, g.cy, g.cz, g.opacity);
+        s_coefA[idx] = make_float4(g.A, g.B, g.Cc, g.D);
+        s_coefB[idx] = make_float2(g.E, g.G);
 #pragma unroll
         for (int c = 0; c < C; ++c) {
           float sn, cs;
@@ -294,13 +299,14 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
       if (lane == 0) atomicAdd(&g_bwd_stats[1], (unsigned long long)total);
 #endif
       for (int jj = 0; jj < total; ++jj) {
-        const BwdG& gg = s_g[jj];
-        const int q = s_pos[jj];
-        const float2 dx = __fadd2_rn(make_float2(gg.mx, gg.mx), npx);
-        const float dy = gg.my - pyf;
-        const bool ny = fabsf(dy) <= gg.ey;
-        const bool n0 = in0 && q < st.last0 && ny && fabsf(dx.x) <= gg.ex;
-        const bool n1 = in1 && q < st.last1 && ny && fabsf(dx.y) <= gg.ex;
+        const float4 geo = s_geo[jj];
+        const float2 wq = s_wq[jj];
+        const int q = __float_as_int(wq.y);
+        const float2 dx = __fadd2_rn(make_float2(geo.x, geo.x), npx);
+        const float dy = geo.y - pyf;
+        const bool ny = fabsf(dy) <= geo.w;
+        const bool n0 = in0 && q < st.last0 && ny && fabsf(dx.x) <= geo.z;
+        const bool n1 = in1 && q < st.last1 && ny && fabsf(dx.y) <= geo.z;
         if (!__any_sync(0xffffffffu, n0 || n1)) {
           if (lane < RL) s_part[warp][jj][lane] = 0.f;
           continue;
@@ -312,7 +318,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         float4 cpx[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) cpx[c] = s_cpx[c][jj];
-        bwd_pair<C>(st, gg, s_w[jj], dx, dy, n0, n1, cpx, v);
+        bwd_pair<C>(st, s_con[jj], wq.x, dx, dy, n0, n1, cpx, v);
 #pragma unroll
         for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
         const float tot = warp_reduce_scatter16(v);
@@ -326,19 +332,21 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         float S[RL];
 #pragma unroll
         for (int k = 0; k < 6; ++k) S[k] = s_part[0][j][k] + s_part[1][j][k] + s_part[2][j][k] + s_part[3][j][k];
-        const BwdG& gg = s_g[j];
-        const float ww = s_w[j];
-        const float ow = gg.opacity * ww;
+        const float4 con = s_con[j];
+        const float4 ca = s_coefA[j];
+        const float2 cb = s_coefB[j];
+        const float ww = s_wq[j].x;
+        const float ow = con.w * ww;
         float val;
-        if (idx == 0) val = -ddelx_dx * ow * (gg.cx * S[1] + gg.cy * S[2]);
-        else if (idx == 1) val = -ddely_dy * ow * (gg.cz * S[2] + gg.cy * S[1]);
+        if (idx == 0) val = -ddelx_dx * ow * (con.x * S[1] + con.y * S[2]);
+        else if (idx == 1) val = -ddely_dy * ow * (con.z * S[2] + con.y * S[1]);
         else if (idx <= 4) {
           const float dcx = -0.5f * ow * S[3], dcy = -0.5f * ow * S[4], dcz = -0.5f * ow * S[5];
-          val = idx == 2 ? dcx * gg.A + dcz * gg.B
-              : idx == 3 ? dcx * gg.Cc + dcy * gg.D + dcz * gg.E
-                         : dcx * gg.B + dcz * gg.G;
+          val = idx == 2 ? dcx * ca.x + dcz * ca.y
+              : idx == 3 ? dcx * ca.z + dcy * ca.w + dcz * cb.x
+                         : dcx * ca.y + dcz * cb.y;
         } else if (idx == 5) val = ww * S[0];
-        else if (idx == 6) val = gg.opacity * S[0];
+        else if (idx == 6) val = con.w * S[0];
         else {
           const int c = idx < 7 + C ? idx - 7 : idx - 7 - C;
           const float X = s_part[0][j][6 + c] + s_part[1][j][6 + c] + s_part[2][j][6 + c] + s_part[3][j][6 + c];

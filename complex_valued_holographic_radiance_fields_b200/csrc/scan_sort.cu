@@ -174,6 +174,8 @@ __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
   if (n_dev) n = min(n, *n_dev);
   __shared__ uint32_t s_wcnt[kOsWarps][256];
   __shared__ uint32_t s_goff[256];
+  __shared__ uint32_t s_bstart[256];
+  __shared__ uint32_t s_key[kOsTile], s_val[kOsTile];
   __shared__ uint32_t sh[33];
   __shared__ int s_tile;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -217,6 +219,8 @@ __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
       s_wcnt[w][d] = run;
       run += c;
     }
+    uint32_t btotal;
+    s_bstart[d] = block_excl_scan(run, btotal, sh);  // start of digit d inside this tile
     uint32_t excl = 0;
     uint32_t* my = status + (size_t)tile * 256 + d;
     if (tile == 0) {
@@ -239,15 +243,25 @@ __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
     s_goff[d] += excl;
   }
   __syncthreads();
+  // order the tile by digit in shared memory, then write each digit's run contiguously
 #pragma unroll
   for (int r = 0; r < kOsItems; ++r) {
     const int i = base + r * 32 + lane;
     if (i < n) {
       const uint32_t d = (key[r] >> shift) & mask;
-      const uint32_t pos = s_goff[d] + s_wcnt[warp][d] + rank[r];
-      kout[pos] = key[r];
-      vout[pos] = val[r];
+      const uint32_t local = s_bstart[d] + s_wcnt[warp][d] + rank[r];
+      s_key[local] = key[r];
+      s_val[local] = val[r];
     }
+  }
+  __syncthreads();
+  const int cnt = min(kOsTile, n - tile * kOsTile);
+  for (int i = tid; i < cnt; i += kOsThreads) {
+    const uint32_t k = s_key[i];
+    const uint32_t d = (k >> shift) & mask;
+    const uint32_t pos = s_goff[d] + (uint32_t)i - s_bstart[d];
+    kout[pos] = k;
+    vout[pos] = s_val[i];
   }
 }
 

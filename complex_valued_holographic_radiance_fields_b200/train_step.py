@@ -150,35 +150,49 @@ class HoloTrainer:
 
     def train_from_host(self, host_targets):
         """One captured iteration per target in `host_targets` (CPU tensors, ideally pinned),
-        returning each iteration's loss as a host float (read after the iteration).  The
-        next target's host->device copy runs on a side stream while the current iteration
-        computes; the iteration itself starts with a device-to-device copy of its target
-        into the graph's input buffer."""
+        returning each iteration's loss as a host float.  Pipelined so the GPU never waits
+        on the host: the next target's host->device copy runs on a side stream during the
+        current iteration, each iteration starts with a device-to-device copy of its target
+        into the graph's input buffer, its loss is copied to pinned host memory right after
+        it, and the host reads loss i once iteration i + 1 has been queued."""
         dev = self.device
         main = torch.cuda.current_stream(dev)
         side = getattr(self, "_copy_stream", None)
         if side is None:
             side = self._copy_stream = torch.cuda.Stream(dev)
             self._staging = torch.empty_like(self._static_target)
-        ready, consumed = torch.cuda.Event(), torch.cuda.Event()
         targets = list(host_targets)
+        n = len(targets)
+        # pinned loss slots and events are kept between calls (allocating pinned memory costs)
+        if getattr(self, "_host_loss", None) is None or self._host_loss.numel() < 2:
+            self._host_loss = torch.empty(2, dtype=torch.float32, pin_memory=True)
+            self._done = [torch.cuda.Event(), torch.cuda.Event()]
+            self._ready, self._consumed = torch.cuda.Event(), torch.cuda.Event()
+        host_loss, done, ready, consumed = self._host_loss, self._done, self._ready, self._consumed
         losses = []
         side.wait_stream(main)
-        if targets:
+        if n:
             with torch.cuda.stream(side):
                 self._staging.copy_(targets[0], non_blocking=True)
                 ready.record(side)
-        for i in range(len(targets)):
+        for i in range(n):
             main.wait_event(ready)
             self._static_target.copy_(self._staging, non_blocking=True)
             consumed.record(main)
-            if i + 1 < len(targets):
+            if i + 1 < n:
                 with torch.cuda.stream(side):
                     side.wait_event(consumed)
                     self._staging.copy_(targets[i + 1], non_blocking=True)
                     ready.record(side)
             self.graph.replay()
-            losses.append(float(self._static_loss.item()))
+            host_loss[i % 2].copy_(self._static_loss, non_blocking=True)
+            done[i % 2].record(main)
+            if i >= 1:
+                done[(i - 1) % 2].synchronize()
+                losses.append(float(host_loss[(i - 1) % 2]))
+        if n:
+            done[(n - 1) % 2].synchronize()
+            losses.append(float(host_loss[(n - 1) % 2]))
         return losses
 
     def graph_overflowed(self):
