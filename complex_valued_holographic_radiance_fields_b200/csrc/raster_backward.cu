@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const float4* __restrict__ rec0, const float4* __restrict__ cov2d, const float* __restrict__ colours,
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
-    float* __restrict__ records) {
+    float* __restrict__ records, const int32_t* __restrict__ tile_order) {
   constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL + 1;
   static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   __shared__ int s_maxlast;
 
   const int VR = 6 + K + 2 * C;
-  const int tile = blockIdx.x;
+  const int tile = tile_order[blockIdx.x];
   const int tx = tile % gx, ty = tile / gx;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int px = tx * kTile + (warp & 1) * 8 + (lane & 3) * 2, py = ty * kTile + (warp >> 1) * 8 + (lane >> 2);
@@ -459,7 +459,8 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
   if (s.N == 0) return CVHRF_OK;
   GeomWs g = carve_geom(const_cast<void*>(geom_ws), geom_bytes, s.N, s.C);
   if (g.bytes == 0 || !geom_ws) return CVHRF_EWORKSPACE;
-  BinWs b = carve_bin(const_cast<void*>(bin_ws), bin_bytes, num_pairs);
+  BinWs b = carve_bin(const_cast<void*>(bin_ws), bin_bytes, num_pairs,
+                      ((s.W + kTile - 1) / kTile) * ((s.H + kTile - 1) / kTile));
   if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
   if (!bwd_ws || bwd_bytes < cvhrf_raster_backward_workspace_bytes(num_pairs, s.K, s.C)) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
@@ -483,7 +484,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
 #define CVHRF_BWD(CC)                                                                                       \
   render_backward_kernel<CC><<<grid, 128, 0, st>>>(rg, pl, b.slot, g.rec0, g.cov2d, s.colours, s.phase,      \
                                                    s.plane_probs, final_Ts, n_contrib, gf, s.K, s.W, s.H,    \
-                                                   cam.grid_x, rec)
+                                                   cam.grid_x, rec, b.tile_order)
     switch (s.C) {
       case 1: CVHRF_BWD(1); break;
       case 2: CVHRF_BWD(2); break;

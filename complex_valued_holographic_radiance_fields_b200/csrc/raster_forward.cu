@@ -137,6 +137,34 @@ __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32
 
 // renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
 //
+// Block -> tile map for the render kernels: tiles by decreasing list length (log2
+// buckets; order inside a bucket is arbitrary), so the longest tiles start first and the
+// last wave holds short ones.  Every tile's output is independent of the order.
+__global__ void __launch_bounds__(1024) tile_order_kernel(const int2* __restrict__ ranges, int T,
+                                                          int32_t* __restrict__ order) {
+  __shared__ int cnt[33];
+  if (threadIdx.x < 33) cnt[threadIdx.x] = 0;
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int w = ranges[t].y - ranges[t].x;
+    atomicAdd(&cnt[w > 0 ? 32 - __clz(w) : 0], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int k = 32; k >= 0; --k) {
+      const int c = cnt[k];
+      cnt[k] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += blockDim.x) {
+    const int w = ranges[t].y - ranges[t].x;
+    order[atomicAdd(&cnt[w > 0 ? 32 - __clz(w) : 0], 1)] = t;
+  }
+}
+
 // One CTA of 64 threads per 16x16 tile; each thread owns four horizontally adjacent
 // pixels as two packed f32x2 pairs (sm_100 FFMA2/FMUL2/FADD2; every lane of a packed
 // operation is an ordinary IEEE-rounded float operation).  The planes are composited
@@ -154,7 +182,8 @@ template <int C>
 __global__ void __launch_bounds__(64) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
     const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs, int K,
-    int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib) {
+    int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib,
+    const int32_t* __restrict__ tile_order) {
   constexpr int NT = 64, NB = 128;
   __shared__ float4 s_mo[NB];      // (mx, mx, my, list position)
   __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
@@ -163,7 +192,7 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
   __shared__ float4 s_col[C][NB];  // (re, re, im, im)
   __shared__ int s_cnt[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int tile = blockIdx.x;
+  const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
   const int px = tx * kTile + (tid & 3) * 4, py = ty * kTile + (tid >> 2);
   const bool rowin = py < H;
@@ -300,11 +329,11 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
 }
 
 int launch_render(int K, int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
-                  const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc) {
+                  const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc, const int32_t* order) {
   switch (C) {
-    case 1: render_forward_kernel<1><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
-    case 2: render_forward_kernel<2><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
-    default: render_forward_kernel<3><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc); break;
+    case 1: render_forward_kernel<1><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
+    case 2: render_forward_kernel<2><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
+    default: render_forward_kernel<3><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
@@ -361,9 +390,10 @@ extern "C" int cvhrf_raster_forward_geometry(const cvhrf_raster_scene* scene, vo
 }
 
 extern "C" size_t cvhrf_raster_binning_workspace_bytes(int N, int num_pairs, int W, int H) {
-  (void)N; (void)W; (void)H;
-  if (num_pairs < 0) return 0;
-  return carve_bin(nullptr, (size_t)-1, num_pairs).bytes + 256;
+  (void)N;
+  if (num_pairs < 0 || W < 1 || H < 1) return 0;
+  const int T = ((W + kTile - 1) / kTile) * ((H + kTile - 1) / kTile);
+  return carve_bin(nullptr, (size_t)-1, num_pairs, T).bytes + 256;
 }
 
 extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
@@ -377,11 +407,11 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
   bool ok;
   GeomWs g = carve_geom_checked(const_cast<void*>(geom_ws), geom_bytes, s.N, s.C, ok);
   if (!ok) return CVHRF_EWORKSPACE;
-  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs);
-  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
-  cudaStream_t st = (cudaStream_t)stream;
   const Camera cam = make_camera(s);
   const int T = cam.grid_x * cam.grid_y;
+  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs, T);
+  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
   int rc;
   clear_ranges_kernel<<<(T + 255) / 256, 256, 0, st>>>((int2*)ranges, T);
   CVHRF_LAUNCH_CHECK();
@@ -405,11 +435,13 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
                                                       visible_indices);
     CVHRF_LAUNCH_CHECK();
   }
+  tile_order_kernel<<<1, 1024, 0, st>>>((const int2*)ranges, T, b.tile_order);
+  CVHRF_LAUNCH_CHECK();
   dim3 grid(T);
   const int2* rg = (const int2*)ranges;
   float2* f = (float2*)field;
   return launch_render(s.K, s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts,
-                       n_contrib);
+                       n_contrib, b.tile_order);
 }
 
 // Same as cvhrf_raster_forward_render without the host round trip: the pair count stays in
@@ -428,11 +460,11 @@ extern "C" int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* sc
   bool ok;
   GeomWs g = carve_geom_checked(const_cast<void*>(geom_ws), geom_bytes, s.N, s.C, ok);
   if (!ok) return CVHRF_EWORKSPACE;
-  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs);
-  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
-  cudaStream_t st = (cudaStream_t)stream;
   const Camera cam = make_camera(s);
   const int T = cam.grid_x * cam.grid_y;
+  BinWs b = carve_bin(bin_ws, bin_bytes, num_pairs, T);
+  if (b.bytes == 0 || !bin_ws) return CVHRF_EWORKSPACE;
+  cudaStream_t st = (cudaStream_t)stream;
   int rc;
   clear_ranges_kernel<<<(T + 255) / 256, 256, 0, st>>>((int2*)ranges, T);
   CVHRF_LAUNCH_CHECK();
@@ -458,9 +490,11 @@ extern "C" int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* sc
                                                            visible_mask);
     CVHRF_LAUNCH_CHECK();
   }
+  tile_order_kernel<<<1, 1024, 0, st>>>((const int2*)ranges, T, b.tile_order);
+  CVHRF_LAUNCH_CHECK();
   dim3 grid(T);
   const int2* rg = (const int2*)ranges;
   float2* f = (float2*)field;
   return launch_render(s.K, s.C, grid, st, rg, point_list, g, s.plane_probs, s.W, s.H, cam.grid_x, f, final_Ts,
-                       n_contrib);
+                       n_contrib, b.tile_order);
 }

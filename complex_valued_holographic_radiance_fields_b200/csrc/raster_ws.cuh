@@ -60,10 +60,11 @@ struct BinWs {
   uint32_t* gauss;     // pairs: Gaussian index of each emission slot
   uint32_t* scratch;
   int32_t* eff;        // capacity mode: pair count if it fits the capacity, else 0
+  int32_t* tile_order; // tiles by decreasing list length: the render kernels' block -> tile map
   size_t bytes;
 };
 
-inline BinWs carve_bin(void* base, size_t cap, int pairs) {
+inline BinWs carve_bin(void* base, size_t cap, int pairs, int tiles) {
   Carver cv(base, cap);
   const int n = pairs > 0 ? pairs : 1;
   BinWs b;
@@ -74,6 +75,7 @@ inline BinWs carve_bin(void* base, size_t cap, int pairs) {
   b.gauss = cv.take<uint32_t>(n);
   b.scratch = cv.take<uint32_t>(sort_scratch_words(n));
   b.eff = cv.take<int32_t>(1);
+  b.tile_order = cv.take<int32_t>(tiles > 0 ? tiles : 1);
   b.bytes = cv.overflow ? 0 : cv.used;
   return b;
 }
