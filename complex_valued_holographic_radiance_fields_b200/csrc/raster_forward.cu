@@ -137,31 +137,49 @@ __global__ void visible_kernel(const float* __restrict__ cam_means, const uint32
 
 // renderTileKernel (forward_splat.cu:101-289), all K planes in one pass.
 //
-// Block -> tile map for the render kernels: tiles by decreasing list length (log2
-// buckets; order inside a bucket is arbitrary), so the longest tiles start first and the
-// last wave holds short ones.  Every tile's output is independent of the order.
+// Block -> tile map for the render kernels: tiles by decreasing list length (1024 buckets
+// of 8 list entries, the longest bucket first; order inside a bucket is arbitrary), so the
+// longest tiles start first and the last wave holds short ones.  Every tile's output is
+// independent of the order.
 __global__ void __launch_bounds__(1024) tile_order_kernel(const int2* __restrict__ ranges, int T,
                                                           int32_t* __restrict__ order) {
-  __shared__ int cnt[33];
-  if (threadIdx.x < 33) cnt[threadIdx.x] = 0;
+  constexpr int NBK = 1024;
+  __shared__ int cnt[NBK];
+  __shared__ uint32_t sh[33];
+  cnt[threadIdx.x] = 0;
   __syncthreads();
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
     const int w = ranges[t].y - ranges[t].x;
-    atomicAdd(&cnt[w > 0 ? 32 - __clz(w) : 0], 1);
+    atomicAdd(&cnt[NBK - 1 - min(w >> 3, NBK - 1)], 1);   // bucket 0 = longest
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int k = 32; k >= 0; --k) {
-      const int c = cnt[k];
-      cnt[k] = run;
-      run += c;
+  {  // exclusive scan of the 1024 bucket counts (warp scans, then over the 32 warp totals)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = cnt[threadIdx.x];
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
     }
+    if (lane == 31) sh[warp] = (uint32_t)inc;
+    __syncthreads();
+    if (warp == 0) {
+      int w = (int)sh[lane], wi = w;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += y;
+      }
+      sh[lane] = (uint32_t)(wi - w);
+    }
+    __syncthreads();
+    cnt[threadIdx.x] = (int)sh[warp] + inc - c;
   }
   __syncthreads();
   for (int t = threadIdx.x; t < T; t += blockDim.x) {
     const int w = ranges[t].y - ranges[t].x;
-    order[atomicAdd(&cnt[w > 0 ? 32 - __clz(w) : 0], 1)] = t;
+    order[atomicAdd(&cnt[NBK - 1 - min(w >> 3, NBK - 1)], 1)] = t;
   }
 }
 
