@@ -372,10 +372,11 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
 // contiguous records with coalesced loads (a half-warp per Gaussian when a record has
 // <= 16 floats, a warp otherwise; lane = record component).  Phase 2: one thread per
 // Gaussian chains the sums through the projection.
-constexpr int kGradBlock = 128;
+constexpr int kGradBlock = 128;    // Gaussians per CTA
+constexpr int kGradThreads = 128;  // threads per CTA: 32 half-warps sum the records, 128 threads chain
 constexpr int kRecMax = 6 + kMaxPlanes + 2 * kMaxChannels;
 
-__global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
+__global__ void __launch_bounds__(kGradThreads) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
                                                                    const float* __restrict__ records, float* gcam,
                                                                    float* gz, float* gq, float* gs, float* gcol,
                                                                    float* gph, float* gop, float* gpl,
@@ -387,21 +388,21 @@ __global__ void __launch_bounds__(kGradBlock) gaussian_grad_kernel(cvhrf_raster_
   const int width = VR <= 16 ? 16 : 32;            // lanes per Gaussian
   const int per_warp = 32 / width;
   const int sub = lane / width, comp = lane - sub * width;
-  for (int lg = warp * per_warp + sub; lg < kGradBlock; lg += (kGradBlock / 32) * per_warp) {
+  for (int lg = warp * per_warp + sub; lg < kGradBlock; lg += (kGradThreads / 32) * per_warp) {
     const int si = s0 + lg;
     float acc = 0.f;
     if (si < s.N && comp < VR) {
       // records exist for slots < max_slot (the pair capacity in capacity mode)
       const uint32_t a = min(si == 0 ? 0u : g.offsets[si - 1], max_slot), b = min(g.offsets[si], max_slot);
       const float* rec = records + (size_t)a * VR + comp;
-#pragma unroll 4
+#pragma unroll 8
       for (uint32_t k = a; k < b; ++k, rec += VR) acc += *rec;
     }
     if (comp < VR) s_r[lg][comp] = acc;
   }
   __syncthreads();
   const int si = s0 + threadIdx.x;
-  if (si >= s.N) return;
+  if (threadIdx.x >= kGradBlock || si >= s.N) return;
   const float* r = s_r[threadIdx.x];
   const uint32_t gi = g.order[si];
   const uint32_t a = min(si == 0 ? 0u : g.offsets[si - 1], max_slot), b = min(g.offsets[si], max_slot);
@@ -493,7 +494,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
 #undef CVHRF_BWD
     CVHRF_LAUNCH_CHECK();
   }
-  gaussian_grad_kernel<<<(s.N + kGradBlock - 1) / kGradBlock, kGradBlock, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
+  gaussian_grad_kernel<<<(s.N + kGradBlock - 1) / kGradBlock, kGradThreads, 0, st>>>(s, cam, g, rec, grad_cam_means, grad_z_vals, grad_quats,
                                                           grad_scales, grad_colours, grad_phase, grad_opacities,
                                                           grad_plane_probs, (uint32_t)num_pairs);
   CVHRF_LAUNCH_CHECK();
