@@ -38,6 +38,10 @@ SIGNATURES = {
                                                  c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                                          c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_adan": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "cvhrf_adan_clip_workspace_bytes": (c_size_t, []),
+    "cvhrf_adan_clip_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "cvhrf_adan_clip_factor": (c_int, [c_void_p, c_int, c_float, c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
     "cvhrf_sort_pairs_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_sort_pairs_u32": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "cvhrf_inclusive_scan_workspace_bytes": (c_size_t, [c_int]),
@@ -75,6 +79,16 @@ class AdamGroup(ctypes.Structure):
     """cvhrf_adam_group (include/cvhrf.h)."""
     _fields_ = [("param", c_void_p), ("grad", c_void_p), ("exp_avg", c_void_p), ("exp_avg_sq", c_void_p),
                 ("N", c_int), ("D", c_int), ("dense", c_int), ("lr", c_float), ("eps", c_float)]
+
+
+class AdanGroup(ctypes.Structure):
+    """cvhrf_adan_group (include/cvhrf.h)."""
+    _fields_ = [(n, c_void_p) for n in ("param", "grad", "exp_avg", "exp_avg_sq", "exp_avg_diff", "neg_pre_grad")] + \
+               [("n", ctypes.c_longlong)] + \
+               [(n, c_float) for n in ("beta1", "beta2", "beta3", "one_minus_beta1", "one_minus_beta2",
+                                       "one_minus_beta3", "bias_correction3_sqrt", "eps", "step_size",
+                                       "step_size_diff", "decay")] + \
+               [("no_prox", c_int), ("first_step", c_int)]
 
 
 class Gaussians(ctypes.Structure):

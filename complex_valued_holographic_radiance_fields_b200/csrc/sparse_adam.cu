@@ -83,19 +83,18 @@ extern "C" int cvhrf_sparse_adam(const cvhrf_adam_group* groups, int ngroups, co
 namespace cvhrf {
 namespace {
 
+// grid (x: grid-stride over the group's elements, y: group); 32-bit element indices
 __global__ void __launch_bounds__(256) sparse_adam_masked_kernel(AdamLaunch L, const uint8_t* __restrict__ mask,
                                                                  int mask_len, float b1, float b2) {
-  const long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= L.start[L.n]) return;
-  int gi = 0;
-#pragma unroll 1
-  while (gi + 1 < L.n && e >= L.start[gi + 1]) ++gi;
-  const cvhrf_adam_group& G = L.g[gi];
-  const long long local = e - L.start[gi];
-  const long long row = local / G.D;
-  if (!G.dense && (row >= mask_len || mask[row] == 0)) return;
-  const size_t idx = (size_t)local;
-  adam_element(G, idx, b1, b2);
+  const cvhrf_adam_group& G = L.g[blockIdx.y];
+  const int n = (int)(L.start[blockIdx.y + 1] - L.start[blockIdx.y]);
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n; e += gridDim.x * blockDim.x) {
+    if (!G.dense) {
+      const int row = e / G.D;
+      if (row >= mask_len || mask[row] == 0) continue;
+    }
+    adam_element(G, (size_t)e, b1, b2);
+  }
 }
 
 __global__ void rows_to_mask_kernel(const int64_t* __restrict__ rows, int V, int mask_len, uint8_t* mask) {
@@ -132,7 +131,12 @@ extern "C" int cvhrf_sparse_adam_masked(const cvhrf_adam_group* groups, int ngro
   }
   L.start[L.n] = tot;
   if (tot == 0) return CVHRF_OK;
-  sparse_adam_masked_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, (cudaStream_t)stream>>>(L, mask, mask_len, b1, b2);
+  long long most = 0;
+  for (int i = 0; i < L.n; ++i) most = L.start[i + 1] - L.start[i] > most ? L.start[i + 1] - L.start[i] : most;
+  if (most >= (1ll << 31)) return CVHRF_EUNSUPPORTED;
+  const long long bx = (most + 255) / 256;
+  dim3 grid((unsigned)(bx < 148 * 4 ? bx : 148 * 4), L.n);
+  sparse_adam_masked_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(L, mask, mask_len, b1, b2);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }

@@ -26,7 +26,7 @@ import torch
 
 from . import scene as SC
 from .loss import intensity_l2_loss
-from .optimizer import SparseGaussianAdam
+from .optimizer import Adan, SparseGaussianAdam
 from .propagation import propagate_planes
 from . import rasterizer as RZ
 from .rasterizer import SplatTileCudaCapacity, splat_tile_cuda
@@ -42,7 +42,7 @@ def plane_distances(K, volume_depth=4e-3, d_val=-2e-3):
 
 class HoloTrainer:
     def __init__(self, N=300000, W=800, H=800, K=3, pitch=8e-6, lr=1e-3, eps=1e-15, seed=0, device="cuda",
-                 camera=None, wavelengths=None, target=None, S=None, frustum=None):
+                 camera=None, wavelengths=None, target=None, S=None, frustum=None, optimizer="sparse_adam"):
         self.device = torch.device(device)
         self.W, self.H, self.K = W, H, K
         self.S = S or max(W, H)   # pad size (train.py: max(W, H) unless configured)
@@ -55,7 +55,17 @@ class HoloTrainer:
         self.params = {k: v.requires_grad_(True) for k, v in
                        SC.make_gaussians(N, K=K, C=len(self.wavelengths), seed=seed, device=self.device,
                                          frustum=frustum).items()}
-        self.opt = SparseGaussianAdam([{"params": [p], "lr": lr} for p in self.params.values()], lr=lr, eps=eps)
+        if optimizer == "adan":
+            # the reference training script's optimizer and per-group learning rates
+            # (utils/optimizer.py:44-65); dense, eager steps only (its scalars change every step)
+            lrs = {"pre_act_scales": 0.005, "pre_act_phase": 0.0025, "colours": 0.0025, "means": lr,
+                   "pre_act_opacities": 0.025, "pre_act_plane_assignment": lr, "pre_act_quats": 0.001}
+            self.opt = Adan([{"params": [p], "lr": lrs[k]} for k, p in self.params.items()], lr=0, eps=1e-8)
+        elif optimizer == "sparse_adam":
+            self.opt = SparseGaussianAdam([{"params": [p], "lr": lr} for p in self.params.values()], lr=lr, eps=eps)
+        else:
+            raise ValueError(f"unknown optimizer {optimizer!r}")
+        self.optimizer = optimizer
         if target is None:
             g = torch.Generator().manual_seed(1)
             target = torch.rand(len(self.wavelengths), self.S, self.S, generator=g)
@@ -92,7 +102,10 @@ class HoloTrainer:
             p.grad = None
         loss, visible = self.forward(target)
         loss.backward()
-        self.opt.step(visible)
+        if self.optimizer == "adan":
+            self.opt.step()
+        else:
+            self.opt.step(visible)
         return loss.detach()
 
     # ---- CUDA-graph mode ------------------------------------------------------------

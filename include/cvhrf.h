@@ -267,6 +267,38 @@ int cvhrf_sparse_adam_masked(const cvhrf_adam_group* groups, int ngroups, const 
                              float beta1, float beta2, void* stream);
 int cvhrf_rows_to_mask(const int64_t* rows, int V, uint8_t* mask, int mask_len, void* stream);
 
+/* ---- Adan (the optimizer of the reference's training script) -------------- */
+/*
+ * One launch for every group (replaces Adan.step, utils/optimizer.py:374-484, with its
+ * foreach kernels :545-611).  The per-step scalars are the caller's and are the ones the
+ * reference hands to torch (computed in double, each rounded to float once):
+ * beta1..3; one_minus_beta1..3 = 1 - beta; bias_correction3_sqrt = sqrt(1 - beta3^step);
+ * step_size = lr / (1 - beta1^step); step_size_diff = lr beta2 / (1 - beta2^step);
+ * decay = 1 - lr wd (no_prox) or 1 + lr wd (otherwise).
+ * first_step = 1 on a group's first step (neg_pre_grad is then taken as -grad).
+ * clip: DEVICE float global-norm clip factor, or NULL for 1 (cvhrf_adan_clip_factor
+ * computes it without a host round trip: min(max_grad_norm / (||all grads|| + eps), 1)).
+ * grad is scaled in place by the clip factor, as the reference's grad.mul_ does.
+ * The clip workspace must be zeroed once (cvhrf_adan_clip_init_workspace).  At most 16 groups.
+ */
+typedef struct {
+  float* param;
+  float* grad;
+  float* exp_avg;
+  float* exp_avg_sq;
+  float* exp_avg_diff;
+  float* neg_pre_grad;
+  long long n;
+  float beta1, beta2, beta3, one_minus_beta1, one_minus_beta2, one_minus_beta3;
+  float bias_correction3_sqrt, eps, step_size, step_size_diff, decay;
+  int no_prox, first_step;
+} cvhrf_adan_group;
+int cvhrf_adan(const cvhrf_adan_group* groups, int ngroups, const float* clip, void* stream);
+size_t cvhrf_adan_clip_workspace_bytes(void);
+int cvhrf_adan_clip_init_workspace(void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_adan_clip_factor(const cvhrf_adan_group* groups, int ngroups, float max_grad_norm, float eps,
+                           float* clip_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- caller glue: filter, depth sort, gather, activations ---------------------- */
 /*
  * Pre-activation Gaussian parameters as the model stores them (model.py:138-169):
