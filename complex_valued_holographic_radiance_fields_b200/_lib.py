@@ -38,6 +38,11 @@ SIGNATURES = {
                                                  c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
                                                          c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_ssim_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "cvhrf_ssim_forward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p, c_void_p,
+                                   c_void_p, c_size_t, c_void_p]),
+    "cvhrf_ssim_backward": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_size_t, c_void_p]),
     "cvhrf_adan": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "cvhrf_adan_clip_workspace_bytes": (c_size_t, []),
     "cvhrf_adan_clip_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),

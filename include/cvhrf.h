@@ -267,6 +267,25 @@ int cvhrf_sparse_adam_masked(const cvhrf_adam_group* groups, int ngroups, const 
                              float beta1, float beta2, void* stream);
 int cvhrf_rows_to_mask(const int64_t* rows, int V, uint8_t* mask, int mask_len, void* stream);
 
+/* ---- fused SSIM (the training loss's SSIM term) ------------------------------ */
+/*
+ * SSIM map of img1 against img2 (C x H x W float32 each, device) with an 11 x 11
+ * Gaussian window (sigma 1.5), zero padding outside the image, constants C1, C2
+ * (the reference uses 0.01^2 and 0.03^2).  Replaces fusedssim / fusedssim_backward
+ * (conv.cu:935-1195) behind FusedSSIMMap / fast_ssim (python_import.py:43-57, 449-454).
+ * cvhrf_ssim_forward writes the map (if map != NULL) and/or its mean (if mean != NULL,
+ * a DEVICE float), and leaves in the workspace what the backward needs.
+ * cvhrf_ssim_backward: gradient with respect to img1 for an upstream gradient given
+ * either per pixel (dL_dmap) or for the mean (dL_dmean, a DEVICE float); exactly one of
+ * the two.  The workspace must be the one the matching forward filled.
+ */
+size_t cvhrf_ssim_workspace_bytes(int C, int H, int W);
+int cvhrf_ssim_forward(const float* img1, const float* img2, int C, int H, int W, float C1, float C2,
+                       float* map, float* mean, void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_ssim_backward(const float* img1, const float* img2, int C, int H, int W,
+                        const float* dL_dmap, const float* dL_dmean, float* grad_img1,
+                        const void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Adan (the optimizer of the reference's training script) -------------- */
 /*
  * One launch for every group (replaces Adan.step, utils/optimizer.py:374-484, with its
