@@ -72,27 +72,44 @@ __global__ void counts_kernel(const uint32_t* offsets, const uint32_t* vis_scan,
   counts[1] = N > 0 ? (int32_t)vis_scan[N - 1] : 0;
 }
 
+// Pairs are written by whole warps: lane j computes Gaussian j's tile rectangle, then the
+// warp writes each of the 32 Gaussians' (tile key, Gaussian) pairs with consecutive lanes
+// on consecutive slots.  The pair's slot is its index, so no slot array is written: the
+// tile sort's first pass takes index values (radix_sort_pairs with v0 == nullptr).
 __global__ void __launch_bounds__(256) emit_pairs_kernel(GeomWs g, Camera cam, int N, BinWs b, uint32_t cap,
                                                          int32_t* overflow) {
   const int si = blockIdx.x * blockDim.x + threadIdx.x;
-  if (si >= N) return;
-  const uint32_t gi = g.order[si];
-  const uint32_t n = g.tiles[gi];
-  if (n == 0) return;
-  uint32_t slot = si == 0 ? 0u : g.offsets[si - 1];
-  if (slot + n > cap) {  // more pairs than the caller's capacity: flag it, emit nothing
-    if (overflow) *overflow = 1;
-    return;
-  }
-  uint2 rmin, rmax;
-  tile_rect(g.means2d[gi], g.radii[gi], cam.grid_x, cam.grid_y, rmin, rmax);
-  for (uint32_t ty = rmin.y; ty < rmax.y; ++ty)
-    for (uint32_t tx = rmin.x; tx < rmax.x; ++tx) {
-      b.tkey[slot] = ty * (uint32_t)cam.grid_x + tx;
-      b.slot[slot] = slot;
-      b.gauss[slot] = gi;
-      ++slot;
+  const int lane = threadIdx.x & 31;
+  uint32_t n = 0, slot = 0, gi = 0;
+  uint2 rmin = make_uint2(0, 0), rmax = make_uint2(0, 0);
+  if (si < N) {
+    gi = g.order[si];
+    n = g.tiles[gi];
+    if (n) {
+      slot = si == 0 ? 0u : g.offsets[si - 1];
+      if (slot + n > cap) {  // more pairs than the caller's capacity: flag it, emit nothing
+        if (overflow) *overflow = 1;
+        n = 0;
+      } else {
+        tile_rect(g.means2d[gi], g.radii[gi], cam.grid_x, cam.grid_y, rmin, rmax);
+      }
     }
+  }
+  unsigned todo = __ballot_sync(0xffffffffu, n != 0);
+  while (todo) {
+    const int j = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const uint32_t nj = __shfl_sync(0xffffffffu, n, j);
+    const uint32_t sj = __shfl_sync(0xffffffffu, slot, j);
+    const uint32_t gj = __shfl_sync(0xffffffffu, gi, j);
+    const uint32_t x0 = __shfl_sync(0xffffffffu, rmin.x, j), y0 = __shfl_sync(0xffffffffu, rmin.y, j);
+    const uint32_t w = __shfl_sync(0xffffffffu, rmax.x, j) - x0;
+    for (uint32_t t = lane; t < nj; t += 32) {
+      const uint32_t ty = t / w, tx = t - ty * w;
+      b.tkey[sj + t] = (y0 + ty) * (uint32_t)cam.grid_x + x0 + tx;
+      b.gauss[sj + t] = gj;
+    }
+  }
 }
 
 __global__ void clear_ranges_kernel(int2* ranges, int T) {
@@ -438,7 +455,7 @@ extern "C" int cvhrf_raster_forward_render(const cvhrf_raster_scene* scene, cons
     CVHRF_LAUNCH_CHECK();
     int alt = 0;
     if ((rc = radix_sort_pairs(b.tkey, b.slot, b.tkey_alt, b.slot_alt, num_pairs, 0, tile_bits(T), b.scratch, st,
-                               &alt)))
+                               &alt, nullptr, nullptr, true)))
       return rc;
     if (alt) {  // keep the sorted result in the primary buffers (the backward reads b.slot)
       CVHRF_CUDA_TRY(cudaMemcpyAsync(b.tkey, b.tkey_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));
@@ -493,7 +510,7 @@ extern "C" int cvhrf_raster_forward_render_capacity(const cvhrf_raster_scene* sc
     CVHRF_LAUNCH_CHECK();
     int alt = 0;
     if ((rc = radix_sort_pairs(b.tkey, b.slot, b.tkey_alt, b.slot_alt, num_pairs, 0, tile_bits(T), b.scratch, st,
-                               &alt, nullptr, b.eff)))
+                               &alt, nullptr, b.eff, true)))
       return rc;
     if (alt) {  // keep the sorted result in the primary buffers (the backward reads b.slot)
       CVHRF_CUDA_TRY(cudaMemcpyAsync(b.tkey, b.tkey_alt, num_pairs * sizeof(uint32_t), cudaMemcpyDeviceToDevice, st));

@@ -167,7 +167,8 @@ __device__ __forceinline__ uint32_t ld_status32(const uint32_t* p) { return *(co
 __device__ __forceinline__ void st_status32(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
 
 __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
-    const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin, uint32_t* __restrict__ kout,
+    const uint32_t* __restrict__ kin, const uint32_t* __restrict__ vin /* null: values = indices */,
+    uint32_t* __restrict__ kout,
     uint32_t* __restrict__ vout, int n, const int* __restrict__ n_dev, const int* __restrict__ skip, int shift,
     int bits, const uint32_t* __restrict__ ghist, uint32_t* __restrict__ status, unsigned* __restrict__ ticket) {
   if (skip && *skip) return;
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
     const int i = base + r * 32 + lane;
     const bool valid = i < n;
     key[r] = valid ? kin[i] : 0u;
-    val[r] = valid ? vin[i] : 0u;
+    val[r] = valid ? (vin ? vin[i] : (uint32_t)i) : 0u;
     const uint32_t d = valid ? (key[r] >> shift) & mask : 256u;
     const unsigned peers = __match_any_sync(0xffffffffu, d);
     uint32_t before = 0;
@@ -302,8 +303,10 @@ size_t sort_scratch_words(int n) {
 }
 
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
-                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip, const int* n_dev) {
+                     uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip, const int* n_dev,
+                     bool index_values) {
   *result_in_alt = 0;
+  if (index_values && skip) return CVHRF_EINVAL;
   if (n <= 1 || end_bit <= begin_bit) return CVHRF_OK;
   if (n > (int)kOsVal) return CVHRF_EUNSUPPORTED;
   const int npass = (end_bit - begin_bit + 7) / 8;
@@ -321,8 +324,9 @@ int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int
   for (int p = 0; p < npass; ++p) {
     const int b = begin_bit + 8 * p;
     const int bits = min(8, end_bit - b);
-    onesweep_pass_kernel<<<nb, kOsThreads, 0, st>>>(ki, vi, ko, vo, n, n_dev, skip, b, bits, ghist + 256 * p,
-                                                    status + (size_t)p * nb * 256, tickets + p);
+    onesweep_pass_kernel<<<nb, kOsThreads, 0, st>>>(ki, (index_values && p == 0) ? nullptr : vi, ko, vo, n, n_dev,
+                                                    skip, b, bits, ghist + 256 * p, status + (size_t)p * nb * 256,
+                                                    tickets + p);
     CVHRF_LAUNCH_CHECK();
     uint32_t* t;
     t = ki; ki = ko; ko = t;

@@ -36,9 +36,10 @@ size_t sort_scratch_words(int n);
 // sort of sorted keys with values 0..n-1 produces.
 int radix_sort_pairs(uint32_t* k0, uint32_t* v0, uint32_t* k1, uint32_t* v1, int n, int begin_bit, int end_bit,
                      uint32_t* scratch, cudaStream_t st, int* result_in_alt, const int* skip = nullptr,
-                     const int* n_dev = nullptr);
+                     const int* n_dev = nullptr, bool index_values = false);
 // (n_dev, when non-null, is a device count: only the first min(n, *n_dev) items are sorted;
-//  n is then the capacity the launch grids are sized for.)
+//  n is then the capacity the launch grids are sized for.  index_values: the values are the
+//  items' indices 0..n-1 and v0's contents are not read; not combined with skip.)
 // *flag = 1 if keys[0..n) is non-decreasing, else 0 (device int, stream-ordered).
 int keys_sorted_flag(const uint32_t* keys, int n, int* flag, cudaStream_t st);
 // Number of look-back waits that ran out of their iteration limit since the library was
