@@ -75,6 +75,7 @@ struct BwdG {
   float cx, cy, cz, ey;           // conic_x, conic_y, conic_z, box half-height
   float A, B, Cc, D;              // d cov / d conic coefficients
   float E, G;
+  float tau;                      // ln(255 opacity w): alpha >= 1/255 needs power >= -tau
 };
 
 // Per-thread state of one plane's back-to-front replay for a horizontal pixel pair
@@ -111,16 +112,20 @@ constexpr int red_len() { return 6 + 2 * C; }
 // (:184-300) for both pixels at once; r[] receives the pair's share of the sums above.
 // A pixel that does not contribute (masked, power > 0, alpha < 1/255) gets alpha = 0 and
 // gd = 0, which leaves its state unchanged exactly (T / 1, 0 P + 1 Q) and adds exact zeros.
-template <int C>
-__device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, float w, float2 dx, float dy, bool n0,
-                                         bool n1, const float4* cpx, float* r) {
-  // con = (conic_x, conic_y, conic_z, opacity)
-  const float2 dy2 = make_float2(dy, dy);
+// power = -0.5 (conic_x dx^2 + conic_z dy^2) - conic_y dx dy for the pixel pair
+__device__ __forceinline__ float2 pair_power(const float4 con, float2 dx, float dy) {
   const float2 cx2 = make_float2(con.x, con.x);
   const float czdd = con.z * dy * dy;
   const float ncydy = -(con.y * dy);
   const float2 quad = __ffma2_rn(__fmul2_rn(cx2, dx), dx, make_float2(czdd, czdd));
-  const float2 power = __ffma2_rn(make_float2(-0.5f, -0.5f), quad, __fmul2_rn(make_float2(ncydy, ncydy), dx));
+  return __ffma2_rn(make_float2(-0.5f, -0.5f), quad, __fmul2_rn(make_float2(ncydy, ncydy), dx));
+}
+
+template <int C>
+__device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, float w, float2 dx, float dy,
+                                         float2 power, bool n0, bool n1, const float4* cpx, float* r) {
+  // con = (conic_x, conic_y, conic_z, opacity); power = pair_power(con, dx, dy)
+  const float2 dy2 = make_float2(dy, dy);
   const float2 G = make_float2(expf(power.x), expf(power.y));
   const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(con.w, con.w), G), make_float2(w, w));
   const float al0 = fminf(0.99f, aw.x), al1 = fminf(0.99f, aw.y);
@@ -176,11 +181,11 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
     float* __restrict__ records, const int32_t* __restrict__ tile_order) {
-  constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL + 1;
+  constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL;
   static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
   __shared__ float4 s_geo[NB];      // (mean x, mean y, box half-width, box half-height): the footprint test
-  __shared__ float2 s_wq[NB];       // (plane weight, list position as int bits)
+  __shared__ float4 s_wq[NB];       // (plane weight, list position as int bits, -ln(255 opacity weight), -)
   __shared__ float4 s_con[NB];      // (conic x, conic y, conic z, opacity): the pixel arithmetic
   __shared__ float4 s_coefA[NB];    // (A, B, Cc, D) and
   __shared__ float2 s_coefB[NB];    // (E, G): d cov / d conic, used once per (tile, Gaussian)
@@ -258,6 +263,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           g.G = (cov.x * det_inv * det_inv) * cov.x;
           // alpha >= 1/255 needs d^T conic d <= 2 ln(255 opacity w): padded box of that ellipse
           const float tau = logf(255.0f * r0.z * w);
+          g.tau = tau;
           const float t2 = 2.0f * fmaxf(tau, 0.0f) * 1.01f;
           g.ex = sqrtf(t2 * fabsf(cov.x)) * 1.01f + 0.05f;
           g.ey = sqrtf(t2 * fabsf(cov.w)) * 1.01f + 0.05f;
@@ -279,7 +285,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         const int idx = off + __popc(bal & lt);
         s_slot[idx] = slot_sorted[range.x + pos];
         s_geo[idx] = make_float4(g.mx, g.my, g.ex, g.ey);
-        s_wq[idx] = make_float2(w, __int_as_float(pos));
+        s_wq[idx] = make_float4(w, __int_as_float(pos), -g.tau - 1e-3f, 0.f);
         s_con[idx] = make_float4(g.cx, g.cy, g.cz, g.opacity);
         s_coefA[idx] = make_float4(g.A, g.B, g.Cc, g.D);
         s_coefB[idx] = make_float2(g.E, g.G);
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
 #endif
       for (int jj = 0; jj < total; ++jj) {
         const float4 geo = s_geo[jj];
-        const float2 wq = s_wq[jj];
+        const float4 wq = s_wq[jj];
         const int q = __float_as_int(wq.y);
         const float2 dx = __fadd2_rn(make_float2(geo.x, geo.x), npx);
         const float dy = geo.y - pyf;
@@ -311,6 +317,17 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           if (lane < RL) s_part[warp][jj][lane] = 0.f;
           continue;
         }
+        // second, exact-footprint vote: alpha >= 1/255 needs power >= -ln(255 opacity w);
+        // the bound carries a 1e-3 margin, so no contributing pixel is dropped (the exact
+        // test is bwd_pair's)
+        const float4 con = s_con[jj];
+        const float2 power = pair_power(con, dx, dy);
+        const bool c0 = n0 && power.x >= wq.z && power.x <= 0.0f;
+        const bool c1 = n1 && power.y >= wq.z && power.y <= 0.0f;
+        if (!__any_sync(0xffffffffu, c0 || c1)) {
+          if (lane < RL) s_part[warp][jj][lane] = 0.f;
+          continue;
+        }
 #ifdef CVHRF_BWD_STATS
         if (lane == 0) atomicAdd(&g_bwd_stats[2], 1ull);
 #endif
@@ -318,7 +335,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         float4 cpx[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) cpx[c] = s_cpx[c][jj];
-        bwd_pair<C>(st, s_con[jj], wq.x, dx, dy, n0, n1, cpx, v);
+        bwd_pair<C>(st, con, wq.x, dx, dy, power, c0, c1, cpx, v);
 #pragma unroll
         for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
         const float tot = warp_reduce_scatter16(v);
