@@ -213,6 +213,10 @@ __global__ void __launch_bounds__(1024) tile_order_kernel(const int2* __restrict
 // through a contribution), so a stopped or off-image pixel just gets alpha = 0: then
 // T (1 - 0) == T and acc + 0 * c == acc exactly.  A plane ends early when every pixel
 // of the tile has stopped in it.
+// ln(2^-26) - 0.1: with power < kFarLog - ln(opacity w), alpha = min(0.99, opacity expf(power) w)
+// stays below 2^-26 even with expf's rounding, so 1 - alpha rounds to 1.0f
+constexpr float kFarLog = -18.0218f - 0.1f;
+
 template <int C>
 __global__ void __launch_bounds__(64) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
@@ -224,6 +228,7 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
   __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
   __shared__ float4 s_c1[NB];      // (i10, i10, i11, i11)
   __shared__ float4 s_ow[NB];      // (o, o, w, w)
+  __shared__ float s_far[NB];      // power below which alpha < 2^-26 (see the far-field skip)
   __shared__ float4 s_col[C][NB];  // (re, re, im, im)
   __shared__ int s_cnt[4];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -282,6 +287,7 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
           s_c0[off] = make_float4(cn.x, cn.x, cn.y, cn.y);
           s_c1[off] = make_float4(cn.z, cn.z, cn.w, cn.w);
           s_ow[off] = make_float4(r0.z, r0.z, w, w);
+          s_far[off] = kFarLog - logf(r0.z * w);
 #pragma unroll
           for (int c = 0; c < C; ++c) {
             const float2 v = cp[(size_t)g * C + c];
@@ -313,6 +319,17 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
         const float2 pB = __fmul2_rn(nh, __ffma2_rn(dxB, uB, __fmul2_rn(dy, vB)));
         const bool aA0 = pA.x <= 0.f && !(TA.x < 1e-4f), aA1 = pA.y <= 0.f && !(TA.y < 1e-4f);
         const bool aB0 = pB.x <= 0.f && !(TB.x < 1e-4f), aB1 = pB.y <= 0.f && !(TB.y < 1e-4f);
+        if (!__any_sync(0xffffffffu, fmaxf(fmaxf(pA.x, pA.y), fmaxf(pB.x, pB.y)) >= s_far[jj])) {
+          // far field for the whole warp: alpha < 2^-26 at every pixel, so T (1 - alpha) == T
+          // exactly and the colour term is below float resolution; only the last-contributor
+          // index moves (the reference counts every Gaussian with power <= 0)
+          const int pos = __float_as_int(mo.w);
+          lA0 = aA0 ? pos : lA0;
+          lA1 = aA1 ? pos : lA1;
+          lB0 = aB0 ? pos : lB0;
+          lB1 = aB1 ? pos : lB1;
+          continue;
+        }
         const float4 ow = s_ow[jj];
         const float2 o2 = make_float2(ow.x, ow.y), w2 = make_float2(ow.z, ow.w);
         const float2 awA = __fmul2_rn(__fmul2_rn(o2, make_float2(expf(pA.x), expf(pA.y))), w2);
