@@ -200,44 +200,45 @@ __global__ void __launch_bounds__(1024) tile_order_kernel(const int2* __restrict
   }
 }
 
-// One CTA of 64 threads per 16x16 tile; each thread owns four horizontally adjacent
-// pixels as two packed f32x2 pairs (sm_100 FFMA2/FMUL2/FADD2; every lane of a packed
-// operation is an ordinary IEEE-rounded float operation).  The planes are composited
-// one after another: for plane p the CTA walks the tile's depth-ordered list in batches
-// of 128, keeps (ballot compaction, order preserved) only the Gaussians whose plane-p
-// weight is >= the cutoff, and front-to-back blends them.  Per pixel this is exactly the
-// reference's chain: power = -0.5 (dx (i00 dx + i10 dy) + dy (i01 dx + i11 dy)),
+// One CTA of 128 threads per 16x16 tile; each thread owns two horizontally adjacent pixels
+// as a packed f32x2 pair (sm_100 FFMA2/FMUL2/FADD2; every lane of a packed operation is an
+// ordinary IEEE-rounded float operation) and each warp an 8 x 8 quadrant.  The planes are
+// composited one after another: for plane p the CTA walks the tile's depth-ordered list in
+// batches of 128, keeps (ballot compaction, order preserved) only the Gaussians whose
+// plane-p weight is >= the cutoff, and front-to-back blends them.  Per pixel this is
+// exactly the reference's chain: power = -0.5 (dx (i00 dx + i10 dy) + dy (i01 dx + i11 dy)),
 // skip if power > 0, G = expf(power), alpha = min(0.99, (o G) w), the pixel takes
 // colour * alpha * T, T' = T (1 - alpha), last = 1-based list position, and stops once
-// T' < 1e-4.  "Stopped" is the same as T < 1e-4 (T starts at 1 and changes only
-// through a contribution), so a stopped or off-image pixel just gets alpha = 0: then
-// T (1 - 0) == T and acc + 0 * c == acc exactly.  A plane ends early when every pixel
-// of the tile has stopped in it.
+// T' < 1e-4.  "Stopped" is the same as T < 1e-4 (T starts at 1 and changes only through
+// a contribution), so a stopped or off-image pixel just gets alpha = 0: then T (1 - 0) == T
+// and acc + 0 * c == acc exactly.  A warp whose 64 pixels have all stopped skips the rest
+// of the plane, and the CTA leaves the plane when all 256 have.
+
 // ln(2^-26) - 0.1: with power < kFarLog - ln(opacity w), alpha = min(0.99, opacity expf(power) w)
 // stays below 2^-26 even with expf's rounding, so 1 - alpha rounds to 1.0f
 constexpr float kFarLog = -18.0218f - 0.1f;
 
 template <int C>
-__global__ void __launch_bounds__(64) render_forward_kernel(
+__global__ void __launch_bounds__(128) render_forward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const float4* __restrict__ rec0,
     const float4* __restrict__ conic, const float2* __restrict__ cp, const float* __restrict__ plane_probs, int K,
     int W, int H, int gx, float2* __restrict__ field, float* __restrict__ final_T, int32_t* __restrict__ n_contrib,
     const int32_t* __restrict__ tile_order) {
-  constexpr int NT = 64, NB = 128;
+  constexpr int NT = 128, NB = 128, NW = 4;
+  static_assert(NB == NT, "one staged Gaussian per thread");
   __shared__ float4 s_mo[NB];      // (mx, mx, my, list position)
   __shared__ float4 s_c0[NB];      // (i00, i00, i01, i01)
   __shared__ float4 s_c1[NB];      // (i10, i10, i11, i11)
   __shared__ float4 s_ow[NB];      // (o, o, w, w)
-  __shared__ float s_far[NB];      // power below which alpha < 2^-26 (see the far-field skip)
+  __shared__ float s_far[NB];      // power below which alpha < 2^-26 (the far-field skip)
   __shared__ float4 s_col[C][NB];  // (re, re, im, im)
-  __shared__ int s_cnt[4];
+  __shared__ int s_cnt[NW];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tile = tile_order ? tile_order[blockIdx.x] : (int)blockIdx.x;
   const int tx = tile % gx, ty = tile / gx;
-  const int px = tx * kTile + (tid & 3) * 4, py = ty * kTile + (tid >> 2);
+  const int px = tx * kTile + (warp & 1) * 8 + (lane & 3) * 2, py = ty * kTile + (warp >> 1) * 8 + (lane >> 2);
   const bool rowin = py < H;
-  const float2 npxA = make_float2(-(float)px, -(float)(px + 1));
-  const float2 npxB = make_float2(-(float)(px + 2), -(float)(px + 3));
+  const float2 npx = make_float2(-(float)px, -(float)(px + 1));
   const float pyf = (float)py;
   const int2 range = ranges[tile];
   const int n = range.y - range.x;
@@ -245,135 +246,101 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
 
   for (int p = 0; p < K; ++p) {
     // off-image pixels start "stopped" (T = 0 < 1e-4) and are never written
-    float2 TA = make_float2(rowin && px < W ? 1.f : 0.f, rowin && px + 1 < W ? 1.f : 0.f);
-    float2 TB = make_float2(rowin && px + 2 < W ? 1.f : 0.f, rowin && px + 3 < W ? 1.f : 0.f);
-    int lA0 = 0, lA1 = 0, lB0 = 0, lB1 = 0;
-    float2 reA[C], imA[C], reB[C], imB[C];
+    float2 T = make_float2(rowin && px < W ? 1.f : 0.f, rowin && px + 1 < W ? 1.f : 0.f);
+    int last0 = 0, last1 = 0;
+    float2 re[C], im[C];
 #pragma unroll
-    for (int c = 0; c < C; ++c) reA[c] = imA[c] = reB[c] = imB[c] = make_float2(0.f, 0.f);
+    for (int c = 0; c < C; ++c) re[c] = im[c] = make_float2(0.f, 0.f);
 
     for (int base = 0; base < n; base += NB) {
-      const bool mine_done = TA.x < 1e-4f && TA.y < 1e-4f && TB.x < 1e-4f && TB.y < 1e-4f;
+      const bool mine_done = T.x < 1e-4f && T.y < 1e-4f;
       if (__syncthreads_and(mine_done)) break;
       // stage: keep this batch's plane-p Gaussians, in list order
-      int gi[2];
-      bool keep[2];
-      unsigned bal[2];
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int j = base + r * NT + tid;
-        keep[r] = false;
-        gi[r] = 0;
-        if (j < n) {
-          gi[r] = point_list[range.x + j];
-          keep[r] = plane_probs[(size_t)gi[r] * K + p] >= kPlaneCutoff;
-        }
-        bal[r] = __ballot_sync(0xffffffffu, keep[r]);
-        if (lane == 0) s_cnt[r * 2 + warp] = __popc(bal[r]);
+      const int j = base + tid;
+      bool keep = false;
+      int gi = 0;
+      if (j < n) {
+        gi = point_list[range.x + j];
+        keep = plane_probs[(size_t)gi * K + p] >= kPlaneCutoff;
       }
+      const unsigned bal = __ballot_sync(0xffffffffu, keep);
+      if (lane == 0) s_cnt[warp] = __popc(bal);
       __syncthreads();
-      const int c0 = s_cnt[0], c1 = s_cnt[1], c2 = s_cnt[2], c3 = s_cnt[3];
-      const unsigned lt = (1u << lane) - 1u;
+      int off = 0, cnt = 0;
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        if (keep[r]) {
-          const int seg = r * 2 + warp;
-          const int off = (seg > 0 ? c0 : 0) + (seg > 1 ? c1 : 0) + (seg > 2 ? c2 : 0) + __popc(bal[r] & lt);
-          const int g = gi[r];
-          const float4 r0 = rec0[g];
-          const float4 cn = conic[g];
-          const float w = plane_probs[(size_t)g * K + p];
-          s_mo[off] = make_float4(r0.x, r0.x, r0.y, __int_as_float(base + r * NT + tid + 1));
-          s_c0[off] = make_float4(cn.x, cn.x, cn.y, cn.y);
-          s_c1[off] = make_float4(cn.z, cn.z, cn.w, cn.w);
-          s_ow[off] = make_float4(r0.z, r0.z, w, w);
-          s_far[off] = kFarLog - logf(r0.z * w);
+      for (int w2 = 0; w2 < NW; ++w2) {
+        off += w2 < warp ? s_cnt[w2] : 0;
+        cnt += s_cnt[w2];
+      }
+      if (keep) {
+        const int o = off + __popc(bal & ((1u << lane) - 1u));
+        const float4 r0 = rec0[gi];
+        const float4 cn = conic[gi];
+        const float w = plane_probs[(size_t)gi * K + p];
+        s_mo[o] = make_float4(r0.x, r0.x, r0.y, __int_as_float(j + 1));
+        s_c0[o] = make_float4(cn.x, cn.x, cn.y, cn.y);
+        s_c1[o] = make_float4(cn.z, cn.z, cn.w, cn.w);
+        s_ow[o] = make_float4(r0.z, r0.z, w, w);
+        s_far[o] = kFarLog - logf(r0.z * w);
 #pragma unroll
-          for (int c = 0; c < C; ++c) {
-            const float2 v = cp[(size_t)g * C + c];
-            s_col[c][off] = make_float4(v.x, v.x, v.y, v.y);
-          }
+        for (int c = 0; c < C; ++c) {
+          const float2 v = cp[(size_t)gi * C + c];
+          s_col[c][o] = make_float4(v.x, v.x, v.y, v.y);
         }
       }
       __syncthreads();
-      const int cnt = c0 + c1 + c2 + c3;
-      // a warp whose 128 pixels have all stopped skips the batch (it only adds exact zeros)
+      // a warp whose 64 pixels have all stopped skips the batch (it only adds exact zeros)
       if (__all_sync(0xffffffffu, mine_done)) continue;
       for (int jj = 0; jj < cnt; ++jj) {
-        if ((jj & 31) == 31 && __all_sync(0xffffffffu, TA.x < 1e-4f && TA.y < 1e-4f && TB.x < 1e-4f && TB.y < 1e-4f))
-          break;
+        if ((jj & 31) == 31 && __all_sync(0xffffffffu, T.x < 1e-4f && T.y < 1e-4f)) break;
         const float4 mo = s_mo[jj];
         const float4 k0 = s_c0[jj], k1 = s_c1[jj];
-        const float2 mx = make_float2(mo.x, mo.y);
         const float dys = mo.z - pyf;
         const float2 dy = make_float2(dys, dys);
-        const float2 t1 = __fmul2_rn(make_float2(k1.x, k1.y), dy);
-        const float2 t2 = __fmul2_rn(make_float2(k1.z, k1.w), dy);
-        const float2 dxA = __fadd2_rn(mx, npxA), dxB = __fadd2_rn(mx, npxB);
-        const float2 uA = __ffma2_rn(make_float2(k0.x, k0.y), dxA, t1);
-        const float2 vA = __ffma2_rn(make_float2(k0.z, k0.w), dxA, t2);
-        const float2 uB = __ffma2_rn(make_float2(k0.x, k0.y), dxB, t1);
-        const float2 vB = __ffma2_rn(make_float2(k0.z, k0.w), dxB, t2);
-        const float2 nh = make_float2(-0.5f, -0.5f);
-        const float2 pA = __fmul2_rn(nh, __ffma2_rn(dxA, uA, __fmul2_rn(dy, vA)));
-        const float2 pB = __fmul2_rn(nh, __ffma2_rn(dxB, uB, __fmul2_rn(dy, vB)));
-        const bool aA0 = pA.x <= 0.f && !(TA.x < 1e-4f), aA1 = pA.y <= 0.f && !(TA.y < 1e-4f);
-        const bool aB0 = pB.x <= 0.f && !(TB.x < 1e-4f), aB1 = pB.y <= 0.f && !(TB.y < 1e-4f);
-        if (!__any_sync(0xffffffffu, fmaxf(fmaxf(pA.x, pA.y), fmaxf(pB.x, pB.y)) >= s_far[jj])) {
+        const float2 dx = __fadd2_rn(make_float2(mo.x, mo.y), npx);
+        const float2 u = __ffma2_rn(make_float2(k0.x, k0.y), dx, __fmul2_rn(make_float2(k1.x, k1.y), dy));
+        const float2 v = __ffma2_rn(make_float2(k0.z, k0.w), dx, __fmul2_rn(make_float2(k1.z, k1.w), dy));
+        const float2 power = __fmul2_rn(make_float2(-0.5f, -0.5f), __ffma2_rn(dx, u, __fmul2_rn(dy, v)));
+        const bool a0 = power.x <= 0.f && !(T.x < 1e-4f), a1 = power.y <= 0.f && !(T.y < 1e-4f);
+        const int pos = __float_as_int(mo.w);
+        if (!__any_sync(0xffffffffu, fmaxf(power.x, power.y) >= s_far[jj])) {
           // far field for the whole warp: alpha < 2^-26 at every pixel, so T (1 - alpha) == T
           // exactly and the colour term is below float resolution; only the last-contributor
           // index moves (the reference counts every Gaussian with power <= 0)
-          const int pos = __float_as_int(mo.w);
-          lA0 = aA0 ? pos : lA0;
-          lA1 = aA1 ? pos : lA1;
-          lB0 = aB0 ? pos : lB0;
-          lB1 = aB1 ? pos : lB1;
+          last0 = a0 ? pos : last0;
+          last1 = a1 ? pos : last1;
           continue;
         }
         const float4 ow = s_ow[jj];
-        const float2 o2 = make_float2(ow.x, ow.y), w2 = make_float2(ow.z, ow.w);
-        const float2 awA = __fmul2_rn(__fmul2_rn(o2, make_float2(expf(pA.x), expf(pA.y))), w2);
-        const float2 awB = __fmul2_rn(__fmul2_rn(o2, make_float2(expf(pB.x), expf(pB.y))), w2);
-        const float2 alA = make_float2(aA0 ? fminf(kMaxAlpha, awA.x) : 0.f, aA1 ? fminf(kMaxAlpha, awA.y) : 0.f);
-        const float2 alB = make_float2(aB0 ? fminf(kMaxAlpha, awB.x) : 0.f, aB1 ? fminf(kMaxAlpha, awB.y) : 0.f);
-        const float2 one = make_float2(1.f, 1.f);
-        const float2 wtA = __fmul2_rn(alA, TA), wtB = __fmul2_rn(alB, TB);
-        TA = __fmul2_rn(TA, __fadd2_rn(one, make_float2(-alA.x, -alA.y)));
-        TB = __fmul2_rn(TB, __fadd2_rn(one, make_float2(-alB.x, -alB.y)));
+        const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(ow.x, ow.y), make_float2(expf(power.x), expf(power.y))),
+                                     make_float2(ow.z, ow.w));
+        const float2 alpha = make_float2(a0 ? fminf(kMaxAlpha, aw.x) : 0.f, a1 ? fminf(kMaxAlpha, aw.y) : 0.f);
+        const float2 wt = __fmul2_rn(alpha, T);
+        T = __fmul2_rn(T, __fadd2_rn(make_float2(1.f, 1.f), make_float2(-alpha.x, -alpha.y)));
 #pragma unroll
         for (int c = 0; c < C; ++c) {
           const float4 col = s_col[c][jj];
-          const float2 cr = make_float2(col.x, col.y), ci = make_float2(col.z, col.w);
-          reA[c] = __ffma2_rn(wtA, cr, reA[c]);
-          imA[c] = __ffma2_rn(wtA, ci, imA[c]);
-          reB[c] = __ffma2_rn(wtB, cr, reB[c]);
-          imB[c] = __ffma2_rn(wtB, ci, imB[c]);
+          re[c] = __ffma2_rn(wt, make_float2(col.x, col.y), re[c]);
+          im[c] = __ffma2_rn(wt, make_float2(col.z, col.w), im[c]);
         }
-        const int pos = __float_as_int(mo.w);
-        lA0 = aA0 ? pos : lA0;
-        lA1 = aA1 ? pos : lA1;
-        lB0 = aB0 ? pos : lB0;
-        lB1 = aB1 ? pos : lB1;
+        last0 = a0 ? pos : last0;
+        last1 = a1 ? pos : last1;
       }
     }
     if (rowin) {
-      const float Tv[4] = {TA.x, TA.y, TB.x, TB.y};
-      const int lv[4] = {lA0, lA1, lB0, lB1};
 #pragma unroll
       for (int c = 0; c < C; ++c) {
-        const float re[4] = {reA[c].x, reA[c].y, reB[c].x, reB[c].y};
-        const float im[4] = {imA[c].x, imA[c].y, imB[c].x, imB[c].y};
         float2* out = field + (size_t)(p * C + c) * HW + pix;
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (px + q < W) out[q] = make_float2(re[q], im[q]);
+        if (px < W) out[0] = make_float2(re[c].x, im[c].x);
+        if (px + 1 < W) out[1] = make_float2(re[c].y, im[c].y);
       }
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        if (px + q < W) {
-          final_T[p * HW + pix + q] = Tv[q];
-          n_contrib[p * HW + pix + q] = lv[q];
-        }
+      if (px < W) {
+        final_T[p * HW + pix] = T.x;
+        n_contrib[p * HW + pix] = last0;
+      }
+      if (px + 1 < W) {
+        final_T[p * HW + pix + 1] = T.y;
+        n_contrib[p * HW + pix + 1] = last1;
       }
     }
     __syncthreads();   // s_* are restaged by the next plane
@@ -383,9 +350,9 @@ __global__ void __launch_bounds__(64) render_forward_kernel(
 int launch_render(int K, int C, dim3 grid, cudaStream_t st, const int2* ranges, const int32_t* pl, const GeomWs& g,
                   const float* pp, int W, int H, int gx, float2* field, float* fT, int32_t* nc, const int32_t* order) {
   switch (C) {
-    case 1: render_forward_kernel<1><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
-    case 2: render_forward_kernel<2><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
-    default: render_forward_kernel<3><<<grid, 64, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
+    case 1: render_forward_kernel<1><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
+    case 2: render_forward_kernel<2><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
+    default: render_forward_kernel<3><<<grid, 128, 0, st>>>(ranges, pl, g.rec0, g.conic, g.cp, pp, K, W, H, gx, field, fT, nc, order); break;
   }
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
