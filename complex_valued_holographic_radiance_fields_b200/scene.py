@@ -238,3 +238,26 @@ def render_inputs_fused(params, camera, owned_planes=0xFFFFFFFF):
               view_matrix=R,
               img_size=(camera.W, camera.H), near_plane=camera.near, far_plane=camera.far)
     return kw, order.long()
+
+
+# ---- checkpoint format (model.py:610-624 save_gaussians) ------------------------------
+
+CHECKPOINT_KEYS = ("pre_act_quats", "means", "pre_act_scales", "colours", "pre_act_phase", "pre_act_opacities",
+                   "pre_act_plane_assignment")
+
+
+def save_gaussians(params, path):
+    """The reference's Gaussian checkpoint: torch.save of a dict of the seven pre-activation
+    parameter tensors, moved to the CPU (model.py:610-624; same keys, same layout)."""
+    torch.save({k: params[k].detach().cpu() for k in CHECKPOINT_KEYS}, path)
+
+
+def load_gaussians(path, device="cuda", requires_grad=True):
+    """Load a checkpoint written by save_gaussians (or by the reference's save_gaussians)
+    as contiguous float32 tensors on `device`."""
+    state = torch.load(path, map_location="cpu")
+    missing = [k for k in CHECKPOINT_KEYS if k not in state]
+    if missing:
+        raise KeyError(f"checkpoint lacks {missing}")
+    return {k: state[k].to(device=device, dtype=torch.float32).contiguous().requires_grad_(requires_grad)
+            for k in CHECKPOINT_KEYS}
