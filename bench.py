@@ -350,6 +350,61 @@ def run_config5(args, world, rank, local):
             "loss": float(loss.item())}
 
 
+METRIC4 = "train iters/sec (8 views per iteration, fwd+bwd+sparse Adam) @500k Gaussians, 1920x1080, K=3"
+CONFIG4 = {"workload": "config4: one iteration = 8 look-at views (radius 4, azimuths 2 pi v / 8, elevation +-20 deg), "
+                       "500k Gaussians, 1920x1080, K=3 planes, 3 wavelengths, 2x-padded ASM propagation (3840^2) at "
+                       "8 um, L2 intensity loss per view, gradients summed, one sparse Adam step",
+           "gaussians": 500000, "image": [1920, 1080], "planes": 3, "pad": 3840, "views": 8,
+           "l2_policy": "inputs larger than L2"}
+
+
+def run_config4(args, world, rank, local):
+    """Multi-view config 4 (strong scaling: the 8 views of an iteration split over the GPUs)."""
+    import math
+    from complex_valued_holographic_radiance_fields_b200 import scene as SC
+    from complex_valued_holographic_radiance_fields_b200.train_step import MultiViewTrainer
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    W, H = 1920, 1080
+    cams = [SC.look_at_camera(W, H, 2 * math.pi * v / 8, math.radians(20.0 if v % 2 == 0 else -20.0))
+            for v in range(8)]
+    tr = MultiViewTrainer(N=500000, W=W, H=H, K=3, S=1920, device=dev, cameras=cams, rank=rank, world=world)
+    graph = os.environ.get("CVHRF_BENCH_EAGER", "0") != "1"
+    if graph:
+        tr.capture(headroom=1.5, warmup=2)
+        step = tr.replay
+    else:
+        step = tr.step
+    for _ in range(args.warmup):
+        step()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        loss = step()
+    t1.record()
+    barrier()
+    if graph and tr.graph_overflowed():
+        raise RuntimeError("pair capacity exceeded during the timed replays")
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    if rank != 0:
+        return None
+    return {"metric": METRIC4, "value": 1000.0 / ms, "unit": "iters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded, config-4 shapes)",
+            "config": dict(CONFIG4, parallelism=f"view-shard{world}", views_on_rank0=tr.views),
+            "execution": "cuda_graph" if graph else "eager", "loss": float(loss.item())}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return None
@@ -374,8 +429,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config3", choices=["config3", "config5"],
-                    help="config3 (default, the BASELINE metric) or config5 (plane-parallel, strong scaling)")
+    ap.add_argument("--workload", default="config3", choices=["config3", "config4", "config5"],
+                    help="config3 (default, the BASELINE metric), config4 (8 views per iteration split over the "
+                         "GPUs) or config5 (planes split over the GPUs); config4/5 scale strongly")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_env()
@@ -387,6 +443,8 @@ def main():
             line = run_reference(args, world, rank)
         elif args.workload == "config5":
             line = run_config5(args, world, rank, local)
+        elif args.workload == "config4":
+            line = run_config4(args, world, rank, local)
         else:
             line = run_mine(args, world, rank, local)
             if line is not None and world == 1 and not args.no_cpu_baseline:

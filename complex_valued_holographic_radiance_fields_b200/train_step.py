@@ -258,3 +258,88 @@ class PlaneShardedTrainer(HoloTrainer):
         else:
             self.opt.step(visible)
         return loss.detach()
+
+
+class MultiViewTrainer(HoloTrainer):
+    """Multi-view training (config 4): one iteration trains on every camera in `cameras`
+    (one seeded target per view), accumulating the Gaussian gradients over the views before
+    one sparse Adam step.  With N processes (one per GPU) the views are split across them
+    (rank r takes views r, r + N, ...) and the gradients and visibility masks are summed
+    with the same exchange as view-parallel training, so an iteration does the same work
+    at any N (strong scaling).  Eager (`step`) and graph-captured (`capture` + `replay`)."""
+
+    def __init__(self, *args, cameras, rank=0, world=1, group=None, **kw):
+        super().__init__(*args, camera=cameras[0], **kw)
+        self.cameras = list(cameras)
+        self.rank, self.world, self.group = rank, world, group
+        self.views = list(range(rank, len(self.cameras), world))
+        C = len(self.wavelengths)
+        self.view_targets = []
+        for v in range(len(self.cameras)):
+            g = torch.Generator().manual_seed(1000 + v)
+            self.view_targets.append(torch.rand(C, self.S, self.S, generator=g).to(self.device))
+        self.max_pairs = 0
+
+    def _exchange(self, flat, mask):
+        import torch.distributed as dist
+        if self.world > 1 and dist.is_initialized():
+            dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+            dist.all_reduce(mask, op=dist.ReduceOp.MAX, group=self.group)
+
+    def _views(self, capacity):
+        n = self.params["means"].shape[0]
+        mask = torch.zeros(n, dtype=torch.uint8, device=self.device)
+        flat, total = None, None
+        for v in self.views:
+            self.camera = self.cameras[v]
+            if capacity:
+                loss, m = self._forward_capacity(self.view_targets[v])
+            else:
+                loss, visible = self.forward(self.view_targets[v])
+                self.max_pairs = max(self.max_pairs, RZ.last_num_pairs)
+                m = torch.zeros(n, dtype=torch.uint8, device=self.device)
+                m[visible] = 1
+            loss.backward()   # gradients accumulate in place into the first view's buffer
+            if flat is None:
+                flat = SC.FusedRenderInputs.last_grad_buffer
+            torch.maximum(mask, m, out=mask)
+            total = loss.detach() if total is None else total + loss.detach()
+        if flat is None:  # no views on this rank: contribute zeros
+            flat = torch.zeros(sum(p.numel() for p in self.params.values()), device=self.device)
+            off = 0
+            for p in self.params.values():
+                p.grad = flat[off:off + p.numel()].view_as(p)
+                off += p.numel()
+            total = torch.zeros((), device=self.device)
+        self._exchange(flat, mask)
+        self.opt.step(row_mask=mask)
+        return total / max(len(self.views), 1)
+
+    def step(self, target=None):
+        for p in self.params.values():
+            p.grad = None
+        return self._views(capacity=False)
+
+    def _step_capacity(self, exchange=None):
+        for p in self.params.values():
+            p.grad = None
+        return self._views(capacity=True)
+
+    def capture(self, headroom=1.5, exchange=None, warmup=2, eager_step=None):
+        self.step()
+        self.pairs_capacity = int(self.max_pairs * headroom) + 4096
+        self._static_target = self.view_targets[0]
+        self._overflow_acc = torch.zeros(1, dtype=torch.int32, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._step_capacity()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self._overflow_acc.zero_()
+        self.graph = torch.cuda.CUDAGraph()
+        launches0 = RZ._lib.lib().cvhrf_kernel_launch_count()
+        with torch.cuda.graph(self.graph):
+            self._static_loss = self._step_capacity()
+        self.graph_launches = RZ._lib.lib().cvhrf_kernel_launch_count() - launches0
+        return self

@@ -98,3 +98,21 @@ def test_train_from_host_matches_eager(cuda):
     assert la == lb
     for k in a.params:
         assert torch.equal(a.params[k], b.params[k]), k
+
+
+def test_multiview_graph_matches_eager(cuda):
+    import math
+    from complex_valued_holographic_radiance_fields_b200.train_step import MultiViewTrainer
+    cams = [SC.look_at_camera(96, 80, 2 * math.pi * v / 3, 0.3 * (v - 1)) for v in range(3)]
+    kw = dict(N=20000, W=96, H=80, K=3, S=96, device=cuda, seed=6, cameras=cams)
+    a, b = MultiViewTrainer(**kw), MultiViewTrainer(**kw)
+    b.capture(headroom=1.5, warmup=2)
+    for _ in range(3):
+        a.step()
+    for _ in range(2):
+        la, lb = a.step(), b.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(la, lb)
+    assert not b.graph_overflowed()
+    for k in a.params:
+        assert torch.equal(a.params[k], b.params[k]), k
