@@ -11,8 +11,9 @@
 //   2. gaussian_grad_kernel: one thread per Gaussian sums its records and chains
 //      d(mean2D), d(cov2D) through the projection (means2d, cov2d, jacobian, cov3d
 //      backward) to the camera-space mean, quaternion and scale.
-// Record layout (VR = 6 + K + 2C floats): dmean.x, dmean.y, dcov_xx, dcov_xy,
-// dcov_yy, dopacity, dplane[K], dcolour[C], dphase[C].
+// Record layout (6 + K + 2C floats, padded to a multiple of 4 so records are float4
+// aligned): dmean.x, dmean.y, dcov_xx, dcov_xy, dcov_yy, dopacity, dplane[K], dcolour[C],
+// dphase[C].
 #include "raster_ws.cuh"
 
 namespace cvhrf {
@@ -26,6 +27,9 @@ __device__ unsigned long long g_bwd_stats[8];
 namespace {
 
 constexpr int kRedV = 16;  // padded length of the per-Gaussian vector that is reduced
+
+// floats per (tile, Gaussian) record: 6 + K + 2C rounded up to a multiple of 4
+__host__ __device__ __forceinline__ int record_stride(int K, int C) { return (6 + K + 2 * C + 3) & ~3; }
 
 // Sum v[0..15] over the warp; afterwards every even lane l holds the total of index (l >> 1).
 __device__ __forceinline__ float warp_reduce_scatter16(float (&v)[kRedV]) {
@@ -195,7 +199,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   __shared__ int s_wcnt[NW];
   __shared__ int s_maxlast;
 
-  const int VR = 6 + K + 2 * C;
+  const int VR = record_stride(K, C);
   const int tile = tile_order[blockIdx.x];
   const int tx = tile % gx, ty = tile / gx;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -391,7 +395,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
 // Gaussian chains the sums through the projection.
 constexpr int kGradBlock = 128;    // Gaussians per CTA
 constexpr int kGradThreads = 128;  // threads per CTA: 32 half-warps sum the records, 128 threads chain
-constexpr int kRecMax = 6 + kMaxPlanes + 2 * kMaxChannels;
+constexpr int kRecMax = (6 + kMaxPlanes + 2 * kMaxChannels + 3) & ~3;
 
 __global__ void __launch_bounds__(kGradThreads) gaussian_grad_kernel(cvhrf_raster_scene s, Camera cam, GeomWs g,
                                                                    const float* __restrict__ records, float* gcam,
@@ -399,23 +403,34 @@ __global__ void __launch_bounds__(kGradThreads) gaussian_grad_kernel(cvhrf_raste
                                                                    float* gph, float* gop, float* gpl,
                                                                    uint32_t max_slot) {
   __shared__ float s_r[kGradBlock][kRecMax + 1];
-  const int K = s.K, C = s.C, VR = 6 + K + 2 * C;
+  const int K = s.K, C = s.C, VR = record_stride(K, C);
   const int s0 = blockIdx.x * kGradBlock;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int width = VR <= 16 ? 16 : 32;            // lanes per Gaussian
-  const int per_warp = 32 / width;
-  const int sub = lane / width, comp = lane - sub * width;
-  for (int lg = warp * per_warp + sub; lg < kGradBlock; lg += (kGradThreads / 32) * per_warp) {
+  // 8 lanes per Gaussian, lane q sums components 4q .. 4q + 3 with float4 loads
+  const int sub = lane >> 3, q = lane & 7;
+  for (int lg = warp * 4 + sub; lg < kGradBlock; lg += (kGradThreads / 32) * 4) {
     const int si = s0 + lg;
-    float acc = 0.f;
-    if (si < s.N && comp < VR) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (si < s.N && 4 * q < VR) {
       // records exist for slots < max_slot (the pair capacity in capacity mode)
       const uint32_t a = min(si == 0 ? 0u : g.offsets[si - 1], max_slot), b = min(g.offsets[si], max_slot);
-      const float* rec = records + (size_t)a * VR + comp;
-#pragma unroll 8
-      for (uint32_t k = a; k < b; ++k, rec += VR) acc += *rec;
+      const float4* rec = reinterpret_cast<const float4*>(records + (size_t)a * VR) + q;
+      const int step = VR >> 2;
+#pragma unroll 4
+      for (uint32_t k = a; k < b; ++k, rec += step) {
+        const float4 v = *rec;
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
     }
-    if (comp < VR) s_r[lg][comp] = acc;
+    if (4 * q < VR) {
+      s_r[lg][4 * q] = acc.x;
+      s_r[lg][4 * q + 1] = acc.y;
+      s_r[lg][4 * q + 2] = acc.z;
+      s_r[lg][4 * q + 3] = acc.w;
+    }
   }
   __syncthreads();
   const int si = s0 + threadIdx.x;
@@ -459,7 +474,7 @@ extern "C" void cvhrf_debug_bwd_stats(unsigned long long* out) {
 extern "C" size_t cvhrf_raster_backward_workspace_bytes(int num_pairs, int K, int C) {
   if (num_pairs < 0 || K < 1 || C < 1) return 0;
   const size_t n = num_pairs > 0 ? num_pairs : 1;
-  return align_up(n * (6 + K + 2 * C) * sizeof(float), 256);
+  return align_up(n * record_stride(K, C) * sizeof(float), 256);
 }
 
 extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void* geom_ws, size_t geom_bytes,
@@ -488,7 +503,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
     const int T = cam.grid_x * cam.grid_y;
     dim3 grid(T);
     const int32_t* pl = point_list;
-    CVHRF_CUDA_TRY(cudaMemsetAsync(rec, 0, (size_t)num_pairs * (6 + s.K + 2 * s.C) * sizeof(float), st));
+    CVHRF_CUDA_TRY(cudaMemsetAsync(rec, 0, (size_t)num_pairs * record_stride(s.K, s.C) * sizeof(float), st));
     const int2* rg = (const int2*)ranges;
     const float2* gf = (const float2*)grad_field;
     // five 45 KB CTAs per SM need the full shared-memory carve-out (set once, before any capture)

@@ -173,6 +173,15 @@ __global__ void __launch_bounds__(kOsThreads) onesweep_pass_kernel(
     int bits, const uint32_t* __restrict__ ghist, uint32_t* __restrict__ status, unsigned* __restrict__ ticket) {
   if (skip && *skip) return;
   if (n_dev) n = min(n, *n_dev);
+  if (n > 0 && ghist[(kin[0] >> shift) & ((1u << bits) - 1u)] == (uint32_t)n) {
+    // every key has the same digit in this pass: the stable order is the identity, so the
+    // pass is a copy (no ranking, no look-back)
+    for (int i = blockIdx.x * kOsThreads + threadIdx.x; i < n; i += gridDim.x * kOsThreads) {
+      kout[i] = kin[i];
+      vout[i] = vin ? vin[i] : (uint32_t)i;
+    }
+    return;
+  }
   __shared__ uint32_t s_wcnt[kOsWarps][256];
   __shared__ uint32_t s_goff[256];
   __shared__ uint32_t s_bstart[256];

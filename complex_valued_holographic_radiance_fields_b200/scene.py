@@ -190,10 +190,12 @@ class FusedRenderInputs(torch.autograd.Function):
         outs = [torch.empty(N, 3, **f32), torch.empty(N, **f32), torch.empty(N, 4, **f32), torch.empty(N, 3, **f32),
                 torch.empty(N, C, **f32), torch.empty(N, C, **f32), torch.empty(N, **f32), torch.empty(N, K, **f32)]
         st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        _lib.check(L.cvhrf_scene_prepare_owned(ctypes.byref(G), R.data_ptr(), T.data_ptr(), float(near), float(far),
-                                               int(owned_planes) & 0xFFFFFFFF, ws.data_ptr(), ws.numel(),
-                                               order.data_ptr(), *[o.data_ptr() for o in outs], st),
-                   "cvhrf_scene_prepare_owned")
+        from .profiling import timed
+        with timed("scene_prepare"):
+            rc = L.cvhrf_scene_prepare_owned(ctypes.byref(G), R.data_ptr(), T.data_ptr(), float(near), float(far),
+                                             int(owned_planes) & 0xFFFFFFFF, ws.data_ptr(), ws.numel(),
+                                             order.data_ptr(), *[o.data_ptr() for o in outs], st)
+        _lib.check(rc, "cvhrf_scene_prepare_owned")
         ctx.save_for_backward(*ins, R, order)
         ctx.mark_non_differentiable(order, outs[1])
         return (*outs, order)
@@ -220,9 +222,11 @@ class FusedRenderInputs(torch.autograd.Function):
             off += t.numel()
         FusedRenderInputs.last_grad_buffer = flat
         st = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
-        _lib.check(_lib.lib().cvhrf_scene_backward(ctypes.byref(G), R.data_ptr(), order.data_ptr(),
-                                                     *[t.data_ptr() for t in gs], *[t.data_ptr() for t in d], st),
-                   "cvhrf_scene_backward")
+        from .profiling import timed
+        with timed("scene_backward"):
+            rc = _lib.lib().cvhrf_scene_backward(ctypes.byref(G), R.data_ptr(), order.data_ptr(),
+                                                 *[t.data_ptr() for t in gs], *[t.data_ptr() for t in d], st)
+        _lib.check(rc, "cvhrf_scene_backward")
         return (*d, None, None, None, None, None)
 
 
