@@ -127,7 +127,7 @@ __device__ __forceinline__ float2 pair_power(const float4 con, float2 dx, float 
 
 template <int C>
 __device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, float w, float2 dx, float dy,
-                                         float2 power, bool n0, bool n1, const float4* cpx, float* r) {
+                                         float2 power, bool n0, bool n1, const float2* cpx, float* r) {
   // con = (conic_x, conic_y, conic_z, opacity); power = pair_power(con, dx, dy)
   const float2 dy2 = make_float2(dy, dy);
   const float2 G = make_float2(expf(power.x), expf(power.y));
@@ -152,8 +152,8 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, flo
   float2 P = make_float2(0.f, 0.f);
 #pragma unroll
   for (int c = 0; c < C; ++c) {
-    P = __ffma2_rn(make_float2(cpx[c].x, cpx[c].y), st.dre[c], P);
-    P = __ffma2_rn(make_float2(cpx[c].z, cpx[c].w), st.dim[c], P);
+    P = __ffma2_rn(make_float2(cpx[c].x, cpx[c].x), st.dre[c], P);
+    P = __ffma2_rn(make_float2(cpx[c].y, cpx[c].y), st.dim[c], P);
     const float2 X = __fmul2_rn(dch, st.dre[c]), Y = __fmul2_rn(dch, st.dim[c]);
     r[6 + c] = X.x + X.y;
     r[6 + C + c] = Y.x + Y.y;
@@ -179,7 +179,7 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, flo
 // for each of those reduces the per-pixel sums over the CTA and adds the pair's share
 // into its record (records start at zero; each pass adds its plane's share).
 template <int C>
-__global__ void __launch_bounds__(128, 5) render_backward_kernel(
+__global__ void __launch_bounds__(128, 6) render_backward_kernel(
     const int2* __restrict__ ranges, const int32_t* __restrict__ point_list, const uint32_t* __restrict__ slot_sorted,
     const float4* __restrict__ rec0, const float4* __restrict__ cov2d, const float* __restrict__ colours,
     const float* __restrict__ phase, const float* __restrict__ plane_probs, const float* __restrict__ final_T,
@@ -189,12 +189,11 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
   static_assert(RL <= kRedV, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
   __shared__ float4 s_geo[NB];      // (mean x, mean y, box half-width, box half-height): the footprint test
-  __shared__ float4 s_wq[NB];       // (plane weight, list position as int bits, -ln(255 opacity weight), -)
+  __shared__ float4 s_wq[NB];       // (plane weight, list position, -ln(255 opacity weight), Gaussian) (ints as bits)
   __shared__ float4 s_con[NB];      // (conic x, conic y, conic z, opacity): the pixel arithmetic
   __shared__ float4 s_coefA[NB];    // (A, B, Cc, D) and
   __shared__ float2 s_coefB[NB];    // (E, G): d cov / d conic, used once per (tile, Gaussian)
-  __shared__ float4 s_cpx[C][NB];   // (re, re, im, im) of colour * e^{i phase}
-  __shared__ float2 s_cs[C][NB];    // (cos, sin)
+  __shared__ float2 s_cpx[C][NB];   // colour * e^{i phase}
   __shared__ float s_part[NW][NB][RP];
   __shared__ int s_wcnt[NW];
   __shared__ int s_maxlast;
@@ -289,7 +288,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         const int idx = off + __popc(bal & lt);
         s_slot[idx] = slot_sorted[range.x + pos];
         s_geo[idx] = make_float4(g.mx, g.my, g.ex, g.ey);
-        s_wq[idx] = make_float4(w, __int_as_float(pos), -g.tau - 1e-3f, 0.f);
+        s_wq[idx] = make_float4(w, __int_as_float(pos), -g.tau - 1e-3f, __int_as_float(gi));
         s_con[idx] = make_float4(g.cx, g.cy, g.cz, g.opacity);
         s_coefA[idx] = make_float4(g.A, g.B, g.Cc, g.D);
         s_coefB[idx] = make_float2(g.E, g.G);
@@ -298,8 +297,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           float sn, cs;
           __sincosf(phase[gi * C + c], &sn, &cs);
           const float col = colours[gi * C + c];
-          s_cs[c][idx] = make_float2(cs, sn);
-          s_cpx[c][idx] = make_float4(col * cs, col * cs, col * sn, col * sn);
+          s_cpx[c][idx] = make_float2(col * cs, col * sn);
         }
       }
       __syncthreads();
@@ -336,7 +334,7 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
         if (lane == 0) atomicAdd(&g_bwd_stats[2], 1ull);
 #endif
         float v[kRedV];
-        float4 cpx[C];
+        float2 cpx[C];
 #pragma unroll
         for (int c = 0; c < C; ++c) cpx[c] = s_cpx[c][jj];
         bwd_pair<C>(st, con, wq.x, dx, dy, power, c0, c1, cpx, v);
@@ -374,11 +372,13 @@ __global__ void __launch_bounds__(128, 5) render_backward_kernel(
           const float Y = s_part[0][j][6 + C + c] + s_part[1][j][6 + C + c] + s_part[2][j][6 + C + c] +
                           s_part[3][j][6 + C + c];
           if (idx < 7 + C) {
-            const float2 cs = s_cs[c][j];
-            val = cs.x * X + cs.y * Y;
+            // cos / sin of the phase recomputed here (same call as at staging) instead of kept
+            float sn, cs;
+            __sincosf(phase[__float_as_int(s_wq[j].w) * C + c], &sn, &cs);
+            val = cs * X + sn * Y;
           } else {
-            const float4 cp = s_cpx[c][j];
-            val = -cp.z * X + cp.x * Y;
+            const float2 cp = s_cpx[c][j];
+            val = -cp.y * X + cp.x * Y;
           }
         }
         const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
@@ -506,7 +506,7 @@ extern "C" int cvhrf_raster_backward(const cvhrf_raster_scene* scene, const void
     CVHRF_CUDA_TRY(cudaMemsetAsync(rec, 0, (size_t)num_pairs * record_stride(s.K, s.C) * sizeof(float), st));
     const int2* rg = (const int2*)ranges;
     const float2* gf = (const float2*)grad_field;
-    // five 45 KB CTAs per SM need the full shared-memory carve-out (set once, before any capture)
+    // six 37 KB CTAs per SM need the full shared-memory carve-out (set once, before any capture)
     static const bool carve = [] {
       cudaFuncSetAttribute(render_backward_kernel<1>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
       cudaFuncSetAttribute(render_backward_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
