@@ -77,6 +77,10 @@ SIGNATURES = {
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_sparse_adam_masked": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_rows_to_mask": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "cvhrf_density_workspace_bytes": (c_size_t, [c_int]),
+    "cvhrf_density_classify": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "cvhrf_density_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "cvhrf_opacity_regularization": (c_int, [c_void_p, c_int, c_float, c_void_p, c_void_p]),
 }
 
 
@@ -101,6 +105,20 @@ class Gaussians(ctypes.Structure):
     _fields_ = [("N", c_int), ("K", c_int), ("C", c_int)] + \
                [(n, c_void_p) for n in ("means", "pre_quats", "pre_scales", "colours", "pre_phase", "pre_opac",
                                         "pre_planes")]
+
+
+class GaussianSet(ctypes.Structure):
+    """cvhrf_gaussian_set (include/cvhrf.h)."""
+    _fields_ = [("N", c_int), ("K", c_int), ("C", c_int)] + \
+               [(n, c_void_p) for n in ("means", "pre_quats", "pre_scales", "colours", "pre_phase", "pre_opac",
+                                        "pre_planes", "grad_means", "grad_pre_quats", "grad_pre_scales",
+                                        "grad_colours", "grad_pre_phase", "grad_pre_opac", "grad_pre_planes")]
+
+
+class DensityParams(ctypes.Structure):
+    """cvhrf_density_params (include/cvhrf.h)."""
+    _fields_ = [(n, c_float) for n in ("grad_threshold", "opacity_threshold", "small_scale_threshold",
+                                       "large_scale_threshold", "split_factor", "clone_offset_factor")]
 
 
 class RasterScene(ctypes.Structure):

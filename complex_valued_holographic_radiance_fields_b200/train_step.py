@@ -25,6 +25,7 @@ sort permutation (``idxs[visible]``) so the update lands on the rows that were s
 import torch
 
 from . import scene as SC
+from .density import density_control, opacity_regularization
 from .loss import intensity_l2_loss
 from .optimizer import Adan, SparseGaussianAdam
 from .propagation import propagate_planes
@@ -55,21 +56,41 @@ class HoloTrainer:
         self.params = {k: v.requires_grad_(True) for k, v in
                        SC.make_gaussians(N, K=K, C=len(self.wavelengths), seed=seed, device=self.device,
                                          frustum=frustum).items()}
-        if optimizer == "adan":
-            # the reference training script's optimizer and per-group learning rates
-            # (utils/optimizer.py:44-65); dense, eager steps only (its scalars change every step)
-            lrs = {"pre_act_scales": 0.005, "pre_act_phase": 0.0025, "colours": 0.0025, "means": lr,
-                   "pre_act_opacities": 0.025, "pre_act_plane_assignment": lr, "pre_act_quats": 0.001}
-            self.opt = Adan([{"params": [p], "lr": lrs[k]} for k, p in self.params.items()], lr=0, eps=1e-8)
-        elif optimizer == "sparse_adam":
-            self.opt = SparseGaussianAdam([{"params": [p], "lr": lr} for p in self.params.values()], lr=lr, eps=eps)
-        else:
+        if optimizer not in ("adan", "sparse_adam"):
             raise ValueError(f"unknown optimizer {optimizer!r}")
-        self.optimizer = optimizer
+        self.optimizer, self.lr, self.eps = optimizer, lr, eps
+        self.opt = self._make_optimizer()
         if target is None:
             g = torch.Generator().manual_seed(1)
             target = torch.rand(len(self.wavelengths), self.S, self.S, generator=g)
         self.target = target.to(self.device)
+
+    def _make_optimizer(self):
+        if self.optimizer == "adan":
+            # the reference training script's optimizer and per-group learning rates
+            # (utils/optimizer.py:44-65); dense, eager steps only (its scalars change every step)
+            lrs = {"pre_act_scales": 0.005, "pre_act_phase": 0.0025, "colours": 0.0025, "means": self.lr,
+                   "pre_act_opacities": 0.025, "pre_act_plane_assignment": self.lr, "pre_act_quats": 0.001}
+            return Adan([{"params": [p], "lr": lrs[k]} for k, p in self.params.items()], lr=0, eps=1e-8)
+        return SparseGaussianAdam([{"params": [p], "lr": self.lr} for p in self.params.values()], lr=self.lr,
+                                  eps=self.eps)
+
+    def densify(self, grad_threshold=0.000005, decrease_amount=0.001, **kw):
+        """The densification block of train.py:327-337, after an optimizer step: density
+        control (clone / split / prune from the last step's gradients), opacity
+        regularisation, and a new optimizer whose per-parameter state is carried over only
+        where the shape did not change (utils/optimizer.py:67-101).  A captured graph is
+        dropped (the Gaussian count changed); call capture() again.  Returns the counts."""
+        old_params, old_opt = self.params, self.opt
+        self.params, counts = density_control(old_params, grad_threshold=grad_threshold, **kw)
+        counts["affected"] = opacity_regularization(self.params, decrease_amount)
+        self.opt = self._make_optimizer()
+        for k, p in self.params.items():
+            q = old_params[k]
+            if p.shape == q.shape and q in old_opt.state:
+                self.opt.state[p] = old_opt.state[q]
+        self.graph = None
+        return counts
 
     # The planes this trainer renders: all of them here; a plane-parallel trainer
     # (PlaneShardedTrainer) renders its share and sums the holograms across GPUs.

@@ -405,6 +405,67 @@ int cvhrf_intensity_loss(const void* holo, const float* target, int n, float* lo
 int cvhrf_intensity_loss_backward(const void* holo, const float* target, int n, const float* grad_loss,
                                   void* grad_holo, void* stream);
 
+
+/* ---- adaptive density control and opacity regularisation ------------------- */
+/*
+ * Gaussians.density_control (model.py:626-1047) on the device.  A Gaussian set is the
+ * seven parameter arrays of cvhrf_gaussians plus their gradients (same shapes;
+ * grad_pre_opac and grad_pre_planes may be null, read as zeros, as the reference does
+ * when those .grad are None).  With g = |grad_means_i|, a = mean_j exp(pre_scales_ij),
+ * o = sigmoid(pre_opac_i):
+ *   keep  = o >= opacity_threshold
+ *   clone = keep & g >= grad_threshold & a < small_scale_threshold
+ *   split = keep & g >= grad_threshold & a > large_scale_threshold
+ * Output rows, in this order: every kept row (unchanged, with its gradient); one clone
+ * per cloned row (means + clone_offset_factor * grad / max(|grad|, 1e-8), opacity
+ * logit(1 - sqrt(1 - o)) as log(c / (1 - c + 1e-6) + 1e-6), gradient copied); then the
+ * first and then the second child of every split row (pre_scales - log(split_factor),
+ * means +/- R(q / |q|) (noise_r * 0.5 * a), gradients halved).  noise is n_split x 3
+ * standard-normal draws (row r for the r-th split row in row order), the draws the
+ * reference takes with torch.randn_like(means_split).
+ *
+ * cvhrf_density_classify writes counts[0..3] (DEVICE u32) = kept, cloned, split and
+ * pruned rows; the output holds counts[0] + counts[1] + 2 counts[2] rows.  The workspace
+ * (cvhrf_density_workspace_bytes(N)) carries the row classification to
+ * cvhrf_density_apply, which writes the output set (out->N = that row count, out->K, C
+ * as in; its gradient pointers must all be non-null).  Output arrays must not overlap
+ * the input ones.
+ */
+typedef struct {
+  int N, K, C;
+  float* means;
+  float* pre_quats;
+  float* pre_scales;
+  float* colours;
+  float* pre_phase;
+  float* pre_opac;
+  float* pre_planes;
+  float* grad_means;
+  float* grad_pre_quats;
+  float* grad_pre_scales;
+  float* grad_colours;
+  float* grad_pre_phase;
+  float* grad_pre_opac;
+  float* grad_pre_planes;
+} cvhrf_gaussian_set;
+
+typedef struct {
+  float grad_threshold, opacity_threshold, small_scale_threshold, large_scale_threshold;
+  float split_factor, clone_offset_factor;
+} cvhrf_density_params;
+
+size_t cvhrf_density_workspace_bytes(int N);
+int cvhrf_density_classify(const cvhrf_gaussian_set* in, const cvhrf_density_params* params, void* workspace,
+                           size_t workspace_bytes, uint32_t* counts, void* stream);
+int cvhrf_density_apply(const cvhrf_gaussian_set* in, const cvhrf_density_params* params, const float* noise,
+                        const void* workspace, size_t workspace_bytes, const cvhrf_gaussian_set* out, void* stream);
+/*
+ * Gaussians.opacity_regularization (model.py:1049-1077), in place: with o =
+ * sigmoid(pre_opac_i), pre_opac_i -= amount / max(o (1 - o), 1e-6); *affected (DEVICE
+ * u32, overwritten) = the number of rows with o > amount.
+ */
+int cvhrf_opacity_regularization(float* pre_opac, int N, float amount, uint32_t* affected, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
