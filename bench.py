@@ -107,7 +107,10 @@ def fp32_peak_tflops(sm_mhz):
 BWD_FLOP_PER_EVAL = 110
 # dram__bytes_read.sum + dram__bytes_write.sum of render_backward_kernel<3> at this workload
 # (profiles/ncu_hot_kernels_config3_train_step.md)
-BWD_NCU_TRAFFIC = 298.1e6
+BWD_NCU_TRAFFIC = 297.1e6
+# the same for the forward propagation's three kernels (rows_forward_s, columns_sum_table_s,
+# rows_inverse_s; profiles/ncu_propagation_config3.md)
+PROP_NCU_TRAFFIC = 413.6e6
 
 
 def peaks():
@@ -225,7 +228,7 @@ def run_mine(args, world, rank, local):
     pbytes = propagation_bytes(K_PLANES, 3, IMG, IMG, IMG)
     roof_prop = {"op": "propagation_forward (3 fused FFT/ASM kernels)", "bound": "hbm",
                  "achieved": pbytes / (prop_ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
-                 "peak_source": hbm_src, "algorithmic_bytes": pbytes, "traffic": None}
+                 "peak_source": hbm_src, "algorithmic_bytes": pbytes, "traffic": PROP_NCU_TRAFFIC}
     roof_prop["frac"] = roof_prop["achieved"] / hbm
     # dominant operator: the rasterizer backward, bound by the FP32 pipe (not HBM, not tensor cores)
     from complex_valued_holographic_radiance_fields_b200 import rasterizer as RZ
