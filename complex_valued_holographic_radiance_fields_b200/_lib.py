@@ -34,6 +34,7 @@ SIGNATURES = {
     "cvhrf_asm_transfer_table_bytes": (c_size_t, [c_int, c_int, c_int]),
     "cvhrf_asm_transfer_table_build": (c_int, [c_void_p, c_int, c_int, c_float_p, c_float_p, c_float, c_float,
                                                c_void_p, c_void_p]),
+    "cvhrf_asm_transfer_table_upload": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "cvhrf_asm_propagate_planes_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p,
                                                  c_void_p, c_size_t, c_void_p]),
     "cvhrf_asm_propagate_planes_adjoint_table": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
@@ -77,6 +78,12 @@ SIGNATURES = {
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_sparse_adam_masked": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_rows_to_mask": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "cvhrf_multiplane_loss_workspace_bytes": (c_size_t, []),
+    "cvhrf_multiplane_loss_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "cvhrf_multiplane_loss": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float_p, c_void_p, c_void_p,
+                                      c_float_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "cvhrf_multiplane_loss_backward": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float_p, c_void_p,
+                                               c_void_p, c_float_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "cvhrf_density_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_density_classify": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),
     "cvhrf_density_apply": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p, c_void_p]),

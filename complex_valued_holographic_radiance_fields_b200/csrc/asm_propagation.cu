@@ -520,6 +520,14 @@ extern "C" int cvhrf_asm_transfer_table_build(const cvhrf_asm_plan* plan, int K,
   return static_transfer_table(d, (float2*)table, tt, K * C, (cudaStream_t)stream);
 }
 
+extern "C" int cvhrf_asm_transfer_table_upload(const cvhrf_asm_plan* plan, int items, const void* centred,
+                                               void* table, void* stream) {
+  if (!plan || !table || !centred || items < 1 || items > kMaxTableItems) return CVHRF_EINVAL;
+  const FftDesc& d = plan->desc;
+  if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
+  return static_transfer_upload(d, (float2*)table, (const float2*)centred, items, (cudaStream_t)stream);
+}
+
 extern "C" int cvhrf_asm_propagate_planes_table(const cvhrf_asm_plan* plan, const void* fields, int K, int C, int H,
                                                 int W, const void* table, void* holo, void* workspace,
                                                 size_t workspace_bytes, void* stream) {

@@ -163,6 +163,27 @@ __global__ void __launch_bounds__(kThreads) transfer_table_s(float2* __restrict_
   }
 }
 
+// Transfer table from a caller's transfer function given in centred (fftshifted) order,
+// Hc[item][y][x] at row bin (y + S) mod P and column bin (x + S) mod P, reordered into the
+// column pass layout of transfer_table_s.
+template <int S>
+__global__ void __launch_bounds__(kThreads) transfer_upload_s(float2* __restrict__ table, const int* __restrict__ digrev,
+                                                             const float2* __restrict__ Hc) {
+  constexpr int P = 2 * S;
+  const int item = blockIdx.y;
+  float2* H = table + (size_t)item * P * P;
+  const float2* src = Hc + (size_t)item * P * P;
+  for (size_t e = (size_t)blockIdx.x * blockDim.x + threadIdx.x; e < (size_t)P * P; e += (size_t)gridDim.x * blockDim.x) {
+    const int q = (int)(e / P), r = (int)(e - (size_t)q * P);
+    const int h = r / S, pos = r - h * S;
+    const int qh = q >= S ? 1 : 0;
+    const int kv = 2 * __ldg(&digrev[q - qh * S]) + qh;
+    const int ku = 2 * __ldg(&digrev[pos]) + h;
+    const int ys = ku >= S ? ku - S : ku + S, xs = kv >= S ? kv - S : kv + S;
+    H[e] = src[(size_t)ys * P + xs];
+  }
+}
+
 // Column pass of a K-plane propagation with a precomputed transfer table: for channel c
 // = blockIdx.y, sum over planes p of H[p, c] * FFT(column of A[p * C + c]) is accumulated
 // in shared memory and inverse-transformed once (the inverse transform is linear), so a
@@ -336,6 +357,15 @@ int run_transfer_table(float2* table, const int* digrev, const TransferTable& tt
   return CVHRF_OK;
 }
 
+template <int S>
+int run_transfer_upload(float2* table, const int* digrev, const float2* Hc, int items, cudaStream_t st) {
+  const size_t n = (size_t)4 * S * S;
+  const size_t nb = (n + kThreads - 1) / kThreads;
+  dim3 grid((unsigned)(nb < 1184 ? nb : 1184), items);
+  transfer_upload_s<S><<<grid, kThreads, 0, st>>>(table, digrev, Hc);
+  CVHRF_LAUNCH_CHECK();
+  return CVHRF_OK;
+}
 
 template <int S>
 int run_columns_table(bool adjoint, const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP,
@@ -425,6 +455,19 @@ int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float
 int static_transfer_table(const FftDesc& d, float2* table, const TransferTable& tt, int items, cudaStream_t st) {
 #define CALL run_transfer_table
 #define ARGS (table, d.digrev, tt, items, st)
+  switch (d.S) {
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
+    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
+    default: return CVHRF_EUNSUPPORTED;
+  }
+#undef CALL
+#undef ARGS
+}
+
+int static_transfer_upload(const FftDesc& d, float2* table, const float2* centred, int items, cudaStream_t st) {
+#define CALL run_transfer_upload
+#define ARGS (table, d.digrev, centred, items, st)
   switch (d.S) {
     case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
     case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;

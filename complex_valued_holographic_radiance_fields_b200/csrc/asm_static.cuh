@@ -93,6 +93,8 @@ int static_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho,
                    cudaStream_t st);
 // Precomputed transfer tables (items x P x P complex64, column-pass layout).
 int static_transfer_table(const FftDesc& d, float2* table, const TransferTable& tt, int items, cudaStream_t st);
+// Table from a caller-supplied transfer function in centred (fftshifted) order, items x P x P.
+int static_transfer_upload(const FftDesc& d, float2* table, const float2* centred, int items, cudaStream_t st);
 // Column pass with a table: adjoint = false sums K planes per channel (A: K*C items,
 // B: C items); adjoint = true scatters each channel to K planes (A: C items, B: K*C).
 int static_columns_table(const FftDesc& d, bool adjoint, const float2* A, int Hi, float2* B, int Ho,

@@ -128,6 +128,18 @@ size_t cvhrf_asm_transfer_table_bytes(int S, int K, int C);
 int cvhrf_asm_transfer_table_build(const cvhrf_asm_plan* plan, int K, int C,
                                    const float* wavelengths, const float* distances,
                                    float pixel_pitch, float aperture, void* table, void* stream);
+/*
+ * A table from a caller-supplied transfer function instead of the built-in one: `centred`
+ * holds `items` (= K*C, item p*C + c) complex64 arrays of (2S)^2 values in centred
+ * (fftshifted) order, row-major, element [y][x] applying to the spectrum bin that
+ * torch.fft.fftshift moves to (y, x); the aperture, if any, is already multiplied in.
+ * This is how a propagator whose kernel comes from elsewhere (odak's
+ * get_propagation_kernel, utils/propagator.py:480-517, cached in self.kernels) runs on
+ * these column passes.  The planes call multiplies by the table; the adjoint call by its
+ * conjugate.
+ */
+int cvhrf_asm_transfer_table_upload(const cvhrf_asm_plan* plan, int items, const void* centred, void* table,
+                                    void* stream);
 int cvhrf_asm_propagate_planes_table(const cvhrf_asm_plan* plan,
                                      const void* fields, int K, int C, int H, int W,
                                      const void* table, void* holo,
@@ -465,6 +477,36 @@ int cvhrf_density_apply(const cvhrf_gaussian_set* in, const cvhrf_density_params
  * u32, overwritten) = the number of rows with o > amount.
  */
 int cvhrf_opacity_regularization(float* pre_opac, int N, float amount, uint32_t* affected, void* stream);
+
+
+/* ---- multiplane reconstruction loss ---------------------------------------- */
+/*
+ * The training loss over the K reconstructed planes (train.py:293-304 with
+ * multiplane_loss_odak.__call__, utils/propagator.py:138-169), in one launch.
+ * fields: K x C x S x S complex64 plane fields (the SLM -> plane propagation's output).
+ * For each plane p, channel c and pixel of the centred H x W crop (odak crop_center:
+ * rows S/2 - H/2 ..., H and W even as in the reference):
+ *   x = clamp(s_c |f|^2, 0, 1),  s_c = channel_scale[c] (HOST, C <= 8; null = 1; the sum
+ *       over frames of the channel's squared laser power, utils/propagator.py:612-634)
+ *   loss = sum over planes of w0 mean((x - t)^2) + w1 mean((x m - t m)^2) + w2 mean((x t - t t)^2)
+ * with targets t and masks m (K x C x H x W float, device), weights w (HOST, 3 floats),
+ * means over C x H x W.  pred (K x C x H x W) receives x; *loss is a DEVICE float.
+ * The workspace (cvhrf_multiplane_loss_workspace_bytes) is zeroed once with
+ * cvhrf_multiplane_loss_init_workspace and left ready by every call (calls sharing it
+ * must be ordered on one stream); the reduction order is fixed (deterministic).
+ * Backward: grad_fields (K x C x S x S, every element written, zero outside the crop)
+ * from *grad_loss (DEVICE float) and an optional extra gradient grad_pred with respect
+ * to pred (K x C x H x W, e.g. from an SSIM term; null = none); clamp passes the
+ * gradient where 0 <= s_c |f|^2 <= 1, as torch.clamp does.
+ */
+size_t cvhrf_multiplane_loss_workspace_bytes(void);
+int cvhrf_multiplane_loss_init_workspace(void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_multiplane_loss(const void* fields, int K, int C, int S, int H, int W, const float* channel_scale,
+                          const float* targets, const float* masks, const float* weights, float* pred, float* loss,
+                          void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_multiplane_loss_backward(const void* fields, int K, int C, int S, int H, int W, const float* channel_scale,
+                                   const float* targets, const float* masks, const float* weights,
+                                   const float* grad_loss, const float* grad_pred, void* grad_fields, void* stream);
 
 #ifdef __cplusplus
 }
