@@ -29,6 +29,7 @@ from .density import density_control, opacity_regularization
 from .loss import intensity_l2_loss
 from .optimizer import Adan, SparseGaussianAdam
 from .propagation import propagate_planes
+from .reconstruction import MultiplaneLoss, Propagator, hologram_training_loss
 from . import rasterizer as RZ
 from .rasterizer import SplatTileCudaCapacity, splat_tile_cuda
 
@@ -43,7 +44,8 @@ def plane_distances(K, volume_depth=4e-3, d_val=-2e-3):
 
 class HoloTrainer:
     def __init__(self, N=300000, W=800, H=800, K=3, pitch=8e-6, lr=1e-3, eps=1e-15, seed=0, device="cuda",
-                 camera=None, wavelengths=None, target=None, S=None, frustum=None, optimizer="sparse_adam"):
+                 camera=None, wavelengths=None, target=None, S=None, frustum=None, optimizer="sparse_adam",
+                 loss="l2", image=None, depth=None):
         self.device = torch.device(device)
         self.W, self.H, self.K = W, H, K
         self.S = S or max(W, H)   # pad size (train.py: max(W, H) unless configured)
@@ -60,7 +62,29 @@ class HoloTrainer:
             raise ValueError(f"unknown optimizer {optimizer!r}")
         self.optimizer, self.lr, self.eps = optimizer, lr, eps
         self.opt = self._make_optimizer()
-        if target is None:
+        if loss not in ("l2", "multiplane"):
+            raise ValueError(f"unknown loss {loss!r}")
+        self.loss_mode = loss
+        if loss == "multiplane":
+            # the training script's loss (train.py:256-304): the hologram is reconstructed at
+            # every depth (utils/propagator.py, configured as train.py:868-883) and scored
+            # against defocus-blurred multiplane targets (utils/data_utils.py:244-259)
+            C = len(self.wavelengths)
+            self.propagator = Propagator(resolution=[self.S, self.S], wavelengths=self.wavelengths,
+                                         pixel_pitch=pitch, number_of_frames=C, number_of_depth_layers=K,
+                                         volume_depth=4e-3, image_location_offset=-2e-3,
+                                         propagator_type="forward", laser_channel_power=torch.eye(C),
+                                         aperture_size=self.aperture, device=self.device)
+            if target is None:
+                g = torch.Generator().manual_seed(1)
+                image = torch.rand(C, H, W, generator=g) if image is None else image
+                depth = torch.rand(1, H, W, generator=g) if depth is None else depth
+                ml = MultiplaneLoss(image, depth, target_blur_size=20, number_of_planes=K, blur_ratio=8,
+                                    weights=[1.0, 1.0, 1.0, 0.0], scheme="defocus", reduction="mean",
+                                    device=self.device)
+                targets, masks, _ = ml.get_targets()
+                target = torch.stack([targets, masks])   # 2 x K x C x H x W: targets, masks
+        elif target is None:
             g = torch.Generator().manual_seed(1)
             target = torch.rand(len(self.wavelengths), self.S, self.S, generator=g)
         self.target = target.to(self.device)
@@ -110,12 +134,17 @@ class HoloTrainer:
     def _combine(self, holo):
         return holo
 
+    def _loss(self, holo, target):
+        if self.loss_mode == "multiplane":
+            return hologram_training_loss(self.propagator, holo, target[0], target[1])
+        return intensity_l2_loss(holo, target)
+
     def forward(self, target=None):
         kw, idxs = self._render_inputs()
         field, visible = splat_tile_cuda(*SC.splat_args(kw))
         holo = self._hologram(field)
         tgt = self.target if target is None else target
-        loss = intensity_l2_loss(holo, tgt)
+        loss = self._loss(holo, tgt)
         return loss, idxs[visible]
 
     def step(self, target=None):
@@ -134,7 +163,7 @@ class HoloTrainer:
         kw, idxs = self._render_inputs()
         field, vis_mask = SplatTileCudaCapacity.apply(*SC.splat_args(kw), self.pairs_capacity)
         holo = self._hologram(field)
-        loss = intensity_l2_loss(holo, target)
+        loss = self._loss(holo, target)
         n = self.params["means"].shape[0]
         row_mask = torch.zeros(n, dtype=torch.uint8, device=self.device)
         row_mask.scatter_(0, idxs, vis_mask)
@@ -264,7 +293,7 @@ class PlaneShardedTrainer(HoloTrainer):
         from .distributed import all_reduce_sum
         C = len(self.wavelengths)
         holo = all_reduce_sum(torch.zeros((C, self.S, self.S), dtype=torch.complex64, device=self.device), self.group)
-        loss = intensity_l2_loss(holo, self.target if target is None else target)
+        loss = self._loss(holo, self.target if target is None else target)
         return loss, torch.empty(0, dtype=torch.long, device=self.device)
 
     def step(self, target=None):

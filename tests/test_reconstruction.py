@@ -195,3 +195,24 @@ def test_gpu_reconstruct_general_powers_matches_torch(cuda):
                 o = torch.fft.ifft2(torch.fft.ifftshift(H[d, c]) * torch.fft.fft2(u))
                 ref[f, d, c] = o[S // 2:S // 2 + S, S // 2:S // 2 + S].abs() ** 2
     assert _rel(r.cpu().numpy(), ref.cpu().numpy()) <= 1e-4
+
+
+@pytest.mark.gpu
+def test_trainer_multiplane_graph_matches_eager(cuda):
+    """The training step with the multiplane reconstruction loss: finite, and the CUDA-graph
+    iteration equal to the eager one bit for bit."""
+    from complex_valued_holographic_radiance_fields_b200.train_step import HoloTrainer
+    kw = dict(N=20000, W=128, H=128, K=3, device=cuda, seed=5, loss="multiplane")
+    a, b = HoloTrainer(**kw), HoloTrainer(**kw)
+    assert a.target.shape == (2, 3, 3, 128, 128)
+    b.capture(headroom=1.5, warmup=2)
+    for _ in range(3):
+        a.step()
+    for _ in range(3):
+        la, lb = a.step(), b.replay()
+        torch.cuda.synchronize()
+        assert torch.isfinite(la)
+        assert torch.equal(la, lb)
+    assert not b.graph_overflowed()
+    for k in a.params:
+        assert torch.equal(a.params[k], b.params[k]), k
