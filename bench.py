@@ -20,6 +20,7 @@ CUDA kernels rebuilt for sm_100a on this GPU (field `reference_cuda_sm100a`).
 import argparse
 import contextlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -439,6 +440,243 @@ def run_reference(args, world, rank):
     return line
 
 
+# ---- component workloads: config 1 (propagation alone), config 2 (rasterizer forward alone)
+METRIC1 = "ASM propagations/s (one field 1024x1024 -> 2048^2 padded, lambda x d sweep)"
+CONFIG1 = {"workload": "config1: 1024x1024 complex64 field (amplitude U[0,1], phase U[0,2pi), seed 0), S=1024 "
+                       "(2048^2 padding), lambda in {639,532,473} nm x d in {-2,0,+2} mm, each P_d then P_-d: "
+                       "18 single-field propagations per step, pitch 8 um, aperture off",
+           "field": [1024, 1024], "pad": 2048, "calls_per_step": 18,
+           "l2_policy": "inputs larger than L2 (each call streams 84 MB)"}
+METRIC2 = "rasterizer forwards/s @100k Gaussians, 800x800, K=3"
+CONFIG2 = {"workload": "config2: splat_tile_cuda forward alone (binning + render), 100k Gaussians, 800x800, K=3 "
+                       "planes, C=3, means U[-1,1]^3 seen by a camera with R = I, T = (0, 0, 4) (seed 0)",
+           "gaussians": 100000, "image": [800, 800], "planes": 3,
+           "l2_policy": "field output 46 MB + binning arrays per call; L2 not flushed"}
+FWD_FLOP_PER_EVAL = 32   # forward convention: d 2, conic 8, alpha and T 6, 3 channels x (re, im) FMA 12
+
+
+def _config1_field():
+    g = torch.Generator().manual_seed(0)
+    a = torch.rand(1024, 1024, generator=g)
+    ph = torch.rand(1024, 1024, generator=g) * 2 * math.pi
+    return torch.polar(a, ph).to(torch.complex64)
+
+
+CONFIG1_CALLS = [(wl, d) for wl in (639e-9, 532e-9, 473e-9) for d in (-2e-3, 0.0, 2e-3)]
+
+
+def _timed_loop(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps
+
+
+def _base_line(metric, config, value, ms, unit, args, world):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded)",
+            "config": dict(config, parallelism=f"replicas{world}" if world > 1 else "single")}
+
+
+def run_config1(args, world, rank, local):
+    from complex_valued_holographic_radiance_fields_b200 import _lib
+    from complex_valued_holographic_radiance_fields_b200.propagation import propagate
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    S = 1024
+    x = _config1_field().to(dev)
+    buf = [torch.empty(S, S, dtype=torch.complex64, device=dev) for _ in range(2)]
+
+    def step(src=None):
+        src = x if src is None else src
+        for wl, d in CONFIG1_CALLS:
+            propagate(src, wl, 8e-6, d, S, -1.0, out=buf[0])
+            propagate(buf[0], wl, 8e-6, -d, S, -1.0, out=buf[1])
+        return buf[1]
+
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    L = _lib.lib()
+    n0 = L.cvhrf_kernel_launch_count()
+    ms = _timed_loop(step, args.steps, args.warmup)
+    launches = (L.cvhrf_kernel_launch_count() - n0) * args.steps // (args.steps + args.warmup)
+    sampler.__exit__()
+    # end to end: the field from pinned host memory and the last output back, every step
+    host_in = x.cpu().pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    dev_in = torch.empty_like(x)
+
+    def e2e_step():
+        dev_in.copy_(host_in, non_blocking=True)
+        host_out.copy_(step(dev_in), non_blocking=True)
+
+    e2e_ms = _timed_loop(e2e_step, args.steps, 2)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return None
+    calls = len(CONFIG1_CALLS) * 2
+    hbm, src = peaks()
+    per_call = 8 * S * S + 16 * S * 2 * S + 16 * S * 2 * S + 8 * S * S   # row, column, inverse-row passes
+    achieved = per_call * calls / (ms * 1e-3) / 1e9
+    line = _base_line(METRIC1, CONFIG1, world * calls * 1000.0 / ms, ms, "propagations/s", args, world)
+    line.update({
+        "e2e": {"value": world * calls * 1000.0 / e2e_ms, "unit": "propagations/s",
+                "h2d_bytes_per_step": host_in.numel() * 8, "d2h_bytes_per_step": host_out.numel() * 8},
+        "gpu_launches": int(launches),
+        "roofline": {"op": "cvhrf_asm_propagate (3 fused FFT/ASM kernels per call)", "bound": "hbm",
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "peak_source": src,
+                     "frac": achieved / hbm, "algorithmic_bytes_per_call": per_call, "traffic": None},
+        "clocks": sampler.summary()})
+    return line
+
+
+def _config2_inputs(dev):
+    from complex_valued_holographic_radiance_fields_b200 import scene as SC
+    cam = SC.PinholeCamera(800, 800)
+    params = SC.make_gaussians(100000, K=3, C=3, seed=0, device=dev)
+    kw, _ = SC.render_inputs(params, cam)
+    return {k: (v.detach().contiguous() if torch.is_tensor(v) else v) for k, v in kw.items()}
+
+
+_KW_TENSORS = ("cam_means_3D", "z_vals", "quats", "scales", "colours", "phase", "opacities", "plane_probs")
+
+
+def run_config2(args, world, rank, local):
+    from complex_valued_holographic_radiance_fields_b200 import _lib, rasterizer as RZ, scene as SC
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    kw = _config2_inputs(dev)
+    sargs = SC.splat_args(kw)
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    L = _lib.lib()
+    n0 = L.cvhrf_kernel_launch_count()
+    ms = _timed_loop(lambda: RZ.splat_tile_cuda(*sargs), args.steps, args.warmup)
+    launches = (L.cvhrf_kernel_launch_count() - n0) * args.steps // (args.steps + args.warmup)
+    sampler.__exit__()
+    pairs = RZ.last_num_pairs
+    # end to end through the same call: the rasterizer inputs from pinned host memory, the field back
+    host = {k: kw[k].cpu().pin_memory() for k in _KW_TENSORS}
+    dkw = dict(kw)
+    for k in _KW_TENSORS:
+        dkw[k] = torch.empty_like(kw[k])
+    field0, _ = RZ.splat_tile_cuda(*sargs)
+    host_out = torch.empty(field0.shape, dtype=field0.dtype).pin_memory()
+
+    def e2e_step():
+        for k in _KW_TENSORS:
+            dkw[k].copy_(host[k], non_blocking=True)
+        f, _ = RZ.splat_tile_cuda(*SC.splat_args(dkw))
+        host_out.copy_(f, non_blocking=True)
+
+    e2e_ms = _timed_loop(e2e_step, args.steps, 2)
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        return None
+    clocks = sampler.summary()
+    sm_mhz = clocks.get("sm_mhz") or 1965.0
+    peak = fp32_peak_tflops(sm_mhz)
+    flop = 256.0 * pairs * FWD_FLOP_PER_EVAL
+    line = _base_line(METRIC2, CONFIG2, world * 1000.0 / ms, ms, "forwards/s", args, world)
+    line.update({
+        "e2e": {"value": world * 1000.0 / e2e_ms, "unit": "forwards/s",
+                "h2d_bytes_per_step": sum(h.numel() * 4 for h in host.values()),
+                "d2h_bytes_per_step": host_out.numel() * 8},
+        "gpu_launches": int(launches),
+        "roofline": {"op": "splat_tile_cuda forward (whole call: binning + render)", "bound": "fp32",
+                     "achieved": flop / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "peak_source": f"SMs x 128 FMA lanes x 2 x median SM clock {sm_mhz:.0f} MHz",
+                     "frac": flop / (ms * 1e-3) / 1e12 / peak,
+                     "work_unit": f"{FWD_FLOP_PER_EVAL} FLOP per pixel-pair evaluation x 256 x {pairs} pairs",
+                     "traffic": None},
+        "clocks": clocks})
+    return line
+
+
+def run_reference_component(args, world, rank):
+    """--impl reference for config1 / config2: the reference's CPU path on the host cores
+    (value), and its CUDA kernels rebuilt for sm_100a on this GPU beside it."""
+    if rank != 0:
+        return None
+    from oracle import cpu_step
+    threads = torch.get_num_threads()
+    if args.workload == "config1":
+        x = _config1_field()
+        sample = CONFIG1_CALLS[:2]
+        t = time.perf_counter()
+        for wl, d in sample:
+            cpu_step.torch_asm(cpu_step.torch_asm(x, wl, 8e-6, d, 1024), wl, 8e-6, -d, 1024)
+        cpu_v = 2 * len(sample) / (time.perf_counter() - t)
+        line = _base_line(METRIC1, CONFIG1, cpu_v, 1000.0 * 18 / cpu_v, "propagations/s", args, world)
+        line["cpu_baseline"] = {"value": cpu_v, "unit": "propagations/s", "cores": threads, "kind": "port",
+                                "sample": f"{2 * len(sample)} propagations: the reference's pure-torch "
+                                          "propagation (python_function.py:35-78) on torch CPU"}
+    else:
+        from oracle import raster_oracle as RO
+        kw = _config2_inputs("cuda" if torch.cuda.is_available() else "cpu")
+        inp = {"cam_means": kw["cam_means_3D"], "z_vals": kw["z_vals"], "quats": kw["quats"],
+               "scales": kw["scales"], "colours": kw["colours"], "phase": kw["phase"], "opacities": kw["opacities"],
+               "plane_probs": kw["plane_probs"], "view": kw["view_matrix"]}
+        inp = {k: v.detach().cpu().numpy() for k, v in inp.items()}
+        t = time.perf_counter()
+        RO.forward(inp, 800, 800, kw["fx"], kw["fy"], kw["px"], kw["py"], kw["near_plane"], kw["far_plane"])
+        cpu_v = 1.0 / (time.perf_counter() - t)
+        threads = cpu_step.num_threads()
+        line = _base_line(METRIC2, CONFIG2, cpu_v, 1000.0 / cpu_v, "forwards/s", args, world)
+        line["cpu_baseline"] = {"value": cpu_v, "unit": "forwards/s", "cores": threads, "kind": "port",
+                                "sample": "1 forward: oracle/raster_oracle.c (OpenMP restatement of the "
+                                          "reference rasterizer)"}
+    line["impl"] = "reference"
+    line["config"]["parallelism"] = "host cpu"
+    line["cpu_baseline"]["cores"] = threads
+    line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    if torch.cuda.is_available():
+        try:
+            line["reference_cuda_sm100a"] = _ref_cuda_component(args)
+        except Exception as e:
+            line["reference_cuda_sm100a"] = {"unavailable": repr(e)[:200]}
+    return line
+
+
+def _ref_cuda_component(args):
+    from oracle import ref_harness
+    if not ref_harness.available():
+        return {"unavailable": "oracle/_ref not built"}
+    steps, warmup = max(min(args.steps, 20), 5), 3
+    if args.workload == "config1":
+        x = _config1_field().cuda()
+        F = ref_harness.RefBandlimitedPropagationFunction
+
+        def step():
+            for wl, d in CONFIG1_CALLS:
+                F.apply(F.apply(x, wl, 8e-6, d, [1024, 1024], -1.0), wl, 8e-6, -d, [1024, 1024], -1.0)
+
+        ms = _timed_loop(step, steps, warmup)
+        return {"value": 18 * 1000.0 / ms, "unit": "propagations/s", "ms_per_step": ms,
+                "what": "reference cuda_modules transfer kernel + torch cuFFT (python_function.py:109-163 glue)"}
+    from complex_valued_holographic_radiance_fields_b200 import scene as SC
+    kw = _config2_inputs("cuda")
+    a = list(SC.splat_args(kw))
+    a[12] = ref_harness.view_buffer(kw["view_matrix"])
+    ms = _timed_loop(lambda: ref_harness.RefSplatTileCuda.apply(*a), steps, warmup)
+    return {"value": 1000.0 / ms, "unit": "forwards/s", "ms_per_step": ms,
+            "what": "reference cov3d_cuda Rasterizer.forward (rebuilt sm_100a)"}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -446,8 +684,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config3", choices=["config3", "config3mp", "config4", "config5"],
-                    help="config3 (default, the BASELINE metric), config3mp (config 3 with the multiplane "
+    ap.add_argument("--workload", default="config3", choices=["config1", "config2", "config3", "config3mp", "config4",
+                                                           "config5"],
+                    help="config1 / config2 (the propagation / rasterizer forward alone), "
+                         "config3 (default, the BASELINE metric), config3mp (config 3 with the multiplane "
                          "reconstruction loss), config4 (8 views per iteration split over the GPUs) or config5 "
                          "(planes split over the GPUs); config4/5 scale strongly")
     args = ap.parse_args()
@@ -457,8 +697,14 @@ def main():
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     try:
-        if args.impl == "reference":
+        if args.impl == "reference" and args.workload in ("config1", "config2"):
+            line = run_reference_component(args, world, rank)
+        elif args.impl == "reference":
             line = run_reference(args, world, rank)
+        elif args.workload == "config1":
+            line = run_config1(args, world, rank, local)
+        elif args.workload == "config2":
+            line = run_config2(args, world, rank, local)
         elif args.workload == "config5":
             line = run_config5(args, world, rank, local)
         elif args.workload == "config4":
