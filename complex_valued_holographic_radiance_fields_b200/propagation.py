@@ -74,8 +74,14 @@ def _workspace(S, in_items, Hi, out_items, Ho, device):
 
 
 def propagate(field, wavelength, pixel_pitch, distance, S, aperture_size=-1.0, out_hw=None, out=None,
-              accumulate=False):
-    """Single propagation: field (Hi, Wi) complex64 -> out (Ho, Wo) (default S x S)."""
+              accumulate=False, use_table=True):
+    """Single propagation: field (Hi, Wi) complex64 -> out (Ho, Wo) (default S x S).
+
+    With `use_table` (and no accumulation), a field propagated to the S x S plane, or an
+    S x S field propagated and cropped back to (Ho, Wo), reads its transfer function from
+    a cached precomputed table (transfer_table, one (2S)^2 table per (wavelength,
+    distance, pitch, aperture)) and runs on the tuned table column pass; the values equal
+    the per-call evaluation.  Other shapes evaluate the transfer function in the call."""
     field = _check_field(field, "field")
     if field.dim() != 2:
         raise ValueError("field must be 2-D (H, W)")
@@ -85,9 +91,31 @@ def propagate(field, wavelength, pixel_pitch, distance, S, aperture_size=-1.0, o
         out = torch.empty((Ho, Wo), dtype=torch.complex64, device=field.device)
     ws = _workspace(S, 1, Hi, 1, Ho, field.device)
     L = _lib.lib()
-    st = L.cvhrf_asm_propagate(get_plan(S, field.device), ctypes.c_void_p(field.data_ptr()), Hi, Wi,
-                               ctypes.c_void_p(out.data_ptr()), Ho, Wo, _scalar(wavelength), _scalar(pixel_pitch),
-                               _scalar(distance), _scalar(aperture_size), int(bool(accumulate)),
+    wl, pitch, d, ap = _scalar(wavelength), _scalar(pixel_pitch), _scalar(distance), _scalar(aperture_size)
+    plan = get_plan(S, field.device)
+    if use_table and not accumulate and ((Ho, Wo) == (S, S) or (Hi, Wi) == (S, S)):
+        if (Ho, Wo) == (S, S):
+            table = transfer_table(S, 1, 1, [wl], [d], pitch, ap, field.device)
+            if table is not None:
+                st = L.cvhrf_asm_propagate_planes_table(plan, ctypes.c_void_p(field.data_ptr()), 1, 1, Hi, Wi,
+                                                        ctypes.c_void_p(table.data_ptr()),
+                                                        ctypes.c_void_p(out.data_ptr()), ctypes.c_void_p(ws.data_ptr()),
+                                                        ws.numel(), _stream(field))
+                _lib.check(st, "cvhrf_asm_propagate_planes_table")
+                return out
+        else:
+            # the adjoint pass multiplies by the conjugate of its table; conj(H at -d) = H at d
+            table = transfer_table(S, 1, 1, [wl], [-d], pitch, ap, field.device)
+            if table is not None:
+                st = L.cvhrf_asm_propagate_planes_adjoint_table(plan, ctypes.c_void_p(field.data_ptr()), 1, 1, Ho,
+                                                                Wo, ctypes.c_void_p(table.data_ptr()),
+                                                                ctypes.c_void_p(out.data_ptr()),
+                                                                ctypes.c_void_p(ws.data_ptr()), ws.numel(),
+                                                                _stream(field))
+                _lib.check(st, "cvhrf_asm_propagate_planes_adjoint_table")
+                return out
+    st = L.cvhrf_asm_propagate(plan, ctypes.c_void_p(field.data_ptr()), Hi, Wi,
+                               ctypes.c_void_p(out.data_ptr()), Ho, Wo, wl, pitch, d, ap, int(bool(accumulate)),
                                ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(field))
     _lib.check(st, "cvhrf_asm_propagate")
     return out

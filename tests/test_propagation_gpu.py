@@ -119,3 +119,19 @@ def test_planes_table_matches_per_call_transfer(cuda, S, H, W, K, C, ap):
     assert P.transfer_table(S, K, C, wl, ds, 8e-6, ap, cuda) is not None
     assert rel(out[0][0], out[1][0]) < 1e-5
     assert rel(out[0][1], out[1][1]) < 1e-5
+
+
+@pytest.mark.parametrize("S,H,W,dist,ap", [(64, 48, 64, -2e-3, -1.0), (256, 200, 256, 3e-3, 100.0),
+                                           (1024, 1024, 1024, 2e-3, -1.0), (800, 800, 800, 0.0, 800.0)])
+def test_single_propagate_table_matches_per_call(cuda, S, H, W, dist, ap):
+    """propagate() reads a cached transfer table for the S x S output (forward) and the S x S
+    input (backward): same results as evaluating the transfer function in the call."""
+    from complex_valued_holographic_radiance_fields_b200.propagation import propagate
+    x = rand_field(H, W, seed=3).to(cuda)
+    a = propagate(x, 532e-9, 8e-6, dist, S, ap, use_table=True)
+    b = propagate(x, 532e-9, 8e-6, dist, S, ap, use_table=False)
+    assert rel(a, b) <= 1e-5
+    g = rand_field(S, S, seed=4).to(cuda)
+    a = propagate(g, 532e-9, 8e-6, -dist, S, ap, out_hw=(H, W), use_table=True)
+    b = propagate(g, 532e-9, 8e-6, -dist, S, ap, out_hw=(H, W), use_table=False)
+    assert rel(a, b) <= 1e-5
