@@ -367,13 +367,22 @@ int run_transfer_upload(float2* table, const int* digrev, const float2* Hc, int 
   return CVHRF_OK;
 }
 
+// Columns per CTA and threads of the table column passes at S = 1024 (build-time choice).
+#ifndef CVHRF_TABLE_COLS_1024
+#define CVHRF_TABLE_COLS_1024 1
+#endif
+#ifndef CVHRF_TABLE_NT_1024
+#define CVHRF_TABLE_NT_1024 128
+#endif
+
 template <int S>
 int run_columns_table(bool adjoint, const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP,
                       const float2* table, int K, int C, cudaStream_t st) {
   // columns per CTA and threads, measured on B200: 3 columns (96 KB, two CTAs per SM) below
   // 1024; one column above, with 128 threads where the radix-32 stages have 64 or 128
   // butterflies per line pair (1024, 2048) and 256 for 1920 (its radix-2 stage is wide)
-  constexpr int COLS = S >= 1024 ? 1 : 3, NT = (S == 1024 || S == 2048) ? 128 : 256;
+  constexpr int COLS = S == 1024 ? CVHRF_TABLE_COLS_1024 : (S > 1024 ? 1 : 3);
+  constexpr int NT = S == 1024 ? CVHRF_TABLE_NT_1024 : (S == 2048 ? 128 : 256);
   dim3 grid((2 * S + COLS - 1) / COLS, C);
   if (!adjoint) {
     const size_t smem = (size_t)COLS * 5 * (S + 1) * sizeof(float2);
