@@ -78,6 +78,12 @@ SIGNATURES = {
     "cvhrf_sparse_adam": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_sparse_adam_masked": (c_int, [c_void_p, c_int, c_void_p, c_int, c_float, c_float, c_void_p]),
     "cvhrf_rows_to_mask": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p]),
+    "cvhrf_hologram_field_workspace_bytes": (c_size_t, []),
+    "cvhrf_hologram_field_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "cvhrf_hologram_field": (c_int, [c_void_p, c_int, ctypes.c_longlong, c_float_p, c_void_p, c_void_p, c_void_p,
+                                     c_size_t, c_void_p]),
+    "cvhrf_hologram_field_backward": (c_int, [c_void_p, c_int, ctypes.c_longlong, c_float_p, c_void_p, c_void_p,
+                                              c_void_p, c_void_p, c_size_t, c_void_p]),
     "cvhrf_multiplane_loss_workspace_bytes": (c_size_t, []),
     "cvhrf_multiplane_loss_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
     "cvhrf_multiplane_loss": (c_int, [c_void_p, c_int, c_int, c_int, c_int, c_int, c_float_p, c_void_p, c_void_p,

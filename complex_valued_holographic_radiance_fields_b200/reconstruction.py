@@ -480,13 +480,70 @@ def reconstruction_loss(fields, targets, masks, weights=(1.0, 1.0, 1.0), channel
     return loss
 
 
+_field_ws = {}
+_field_ws_lock = threading.Lock()
+
+
+def _field_workspace(device):
+    key = torch.device(device)
+    with _field_ws_lock:
+        w = _field_ws.get(key)
+        if w is None:
+            L = _lib.lib()
+            n = L.cvhrf_hologram_field_workspace_bytes()
+            w = torch.empty(n, dtype=torch.uint8, device=device)
+            _lib.check(L.cvhrf_hologram_field_init_workspace(ctypes.c_void_p(w.data_ptr()), n, _stream(w)),
+                       "cvhrf_hologram_field_init_workspace")
+            _field_ws[key] = w
+    return w
+
+
+class HologramFieldFunction(torch.autograd.Function):
+    """hologram (C, S, S) complex64 -> SLM field |h| exp(i (angle(h) mod 2 pi - mean) s_c)
+    (train.py:280-283 and utils/propagator.py:612-620) in two libcvhrf launches each way."""
+
+    @staticmethod
+    def forward(ctx, holo, phase_scale):
+        holo = _check_field(holo, "hologram")
+        C = holo.shape[0]
+        n = holo[0].numel()
+        field = torch.empty_like(holo)
+        mean = torch.empty((), dtype=torch.float32, device=holo.device)
+        ws = _field_workspace(holo.device)
+        with timed("hologram_field"):
+            _lib.check(_lib.lib().cvhrf_hologram_field(
+                ctypes.c_void_p(holo.data_ptr()), C, n, _lib.float_array(phase_scale), ctypes.c_void_p(field.data_ptr()),
+                ctypes.c_void_p(mean.data_ptr()), ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(holo)),
+                "cvhrf_hologram_field")
+        ctx.save_for_backward(holo, mean)
+        ctx.scale = list(phase_scale)
+        return field
+
+    @staticmethod
+    def backward(ctx, g):
+        holo, mean = ctx.saved_tensors
+        g = _check_field(g, "grad")
+        grad = torch.empty_like(holo)
+        ws = _field_workspace(holo.device)
+        with timed("hologram_field_backward"):
+            _lib.check(_lib.lib().cvhrf_hologram_field_backward(
+                ctypes.c_void_p(holo.data_ptr()), holo.shape[0], holo[0].numel(), _lib.float_array(ctx.scale),
+                ctypes.c_void_p(mean.data_ptr()), ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(grad.data_ptr()),
+                ctypes.c_void_p(ws.data_ptr()), ws.numel(), _stream(holo)), "cvhrf_hologram_field_backward")
+        return grad, None
+
+
 def hologram_training_loss(prop, hologram, targets, masks, weights=(1.0, 1.0, 1.0), ssim=True, lambda_ssim=0.025):
     """train.py:280-304 after the render: the hologram's phase (mod 2 pi, minus its mean)
-    and amplitude are recombined, reconstructed at every depth (prop: a Propagator with
-    one channel per frame) and scored by reconstruction_loss.  hologram: C x S x S
-    complex64 (differentiable)."""
-    phase = torch.remainder(torch.angle(hologram), 2 * np.pi)
-    amplitude = torch.abs(hologram)
-    phase = phase - phase.mean()
-    fields = prop.propagate_all(prop.hologram_field(phase, amplitude))
+    and amplitude are recombined (HologramFieldFunction), reconstructed at every depth
+    (prop: a Propagator with one channel per frame) and scored by reconstruction_loss.
+    hologram: C x S x S complex64 (differentiable)."""
+    C = prop.number_of_channels
+    # the phase scale as host floats, read once (a device read here would synchronise,
+    # and cannot happen inside a captured graph)
+    key = prop.phase_scale.data_ptr()
+    if getattr(prop, "_scale_key", None) != key:
+        prop._scale_list = prop.phase_scale.detach().float().cpu()[:C].tolist()
+        prop._scale_key = key
+    fields = prop.propagate_all(HologramFieldFunction.apply(hologram, prop._scale_list))
     return reconstruction_loss(fields, targets, masks, weights, prop.channel_scale().tolist(), ssim, lambda_ssim)

@@ -508,6 +508,27 @@ int cvhrf_multiplane_loss_backward(const void* fields, int K, int C, int S, int 
                                    const float* targets, const float* masks, const float* weights,
                                    const float* grad_loss, const float* grad_pred, void* grad_fields, void* stream);
 
+
+/* ---- hologram -> SLM field of the training loss ------------------------------ */
+/*
+ * train.py:280-283 with the field formation of utils/propagator.py:612-620, fused: for
+ * the C x n complex64 hologram h (channel-major),
+ *   phi = angle(h) mod 2 pi, m = mean of phi over all C n values, field[c] = |h| exp(i (phi - m) s_c)
+ * with s_c = phase_scale[c] (HOST, C <= 8; null = 1).  *mean (DEVICE float) receives m and
+ * is passed back to the backward, which writes grad_holo (torch's complex-gradient
+ * convention; zero where h = 0) from grad_field.  The workspace
+ * (cvhrf_hologram_field_workspace_bytes) is zeroed once with
+ * cvhrf_hologram_field_init_workspace and left ready by every call; calls sharing it must
+ * be ordered on one stream.  Reductions are in a fixed order (deterministic).
+ */
+size_t cvhrf_hologram_field_workspace_bytes(void);
+int cvhrf_hologram_field_init_workspace(void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_hologram_field(const void* holo, int C, long long n, const float* phase_scale, void* field, float* mean,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int cvhrf_hologram_field_backward(const void* holo, int C, long long n, const float* phase_scale, const float* mean,
+                                  const void* grad_field, void* grad_holo, void* workspace, size_t workspace_bytes,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -216,3 +216,27 @@ def test_trainer_multiplane_graph_matches_eager(cuda):
     assert not b.graph_overflowed()
     for k in a.params:
         assert torch.equal(a.params[k], b.params[k]), k
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("C,S,scale", [(3, 64, (1.0, 1.0, 1.0)), (3, 200, (1.0, 0.8, 1.2)), (1, 128, (0.5,))])
+def test_gpu_hologram_field_matches_torch(cuda, C, S, scale):
+    """The fused hologram -> SLM field step against train.py:280-283's torch ops (with
+    exact zeros in the hologram, where both give a zero gradient)."""
+    from complex_valued_holographic_radiance_fields_b200.reconstruction import HologramFieldFunction
+    g = torch.Generator(device=cuda).manual_seed(C * 7 + S)
+    h = torch.view_as_complex(torch.randn(C, S, S, 2, generator=g, device=cuda)).contiguous()
+    h[0, :3, :5] = 0
+    up = torch.view_as_complex(torch.randn(C, S, S, 2, generator=g, device=cuda)).contiguous()
+    a = h.clone().requires_grad_(True)
+    fa = HologramFieldFunction.apply(a, list(scale))
+    fa.backward(up)
+    b = h.clone().requires_grad_(True)
+    phase = torch.remainder(torch.angle(b), 2 * np.pi)
+    phase = phase - phase.mean()
+    sc = torch.tensor(scale, device=cuda).view(C, 1, 1)
+    fb = torch.polar(torch.abs(b), phase * sc)
+    fb.backward(up)
+    assert _rel(fa.detach().cpu().numpy(), fb.detach().cpu().numpy()) <= 1e-5
+    gb = torch.nan_to_num(b.grad)
+    assert _rel(a.grad.cpu().numpy(), gb.cpu().numpy()) <= 1e-4
