@@ -272,9 +272,13 @@ def run_mine(args, world, rank, local):
     return line
 
 
-def cpu_baseline(samples=1):
+def cpu_baseline(samples=3, warmup=1):
+    """The config-3 step on the host cores: `warmup` untimed steps, then the median of
+    `samples` timed ones."""
     from oracle.cpu_step import CpuHoloStep, num_threads
     st = CpuHoloStep(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES)
+    for _ in range(warmup):
+        st.step()
     ts = []
     for _ in range(samples):
         t = time.perf_counter()
@@ -282,9 +286,10 @@ def cpu_baseline(samples=1):
         ts.append(time.perf_counter() - t)
     v = 1.0 / statistics.median(ts)
     return {"value": v, "unit": "iters/s", "cores": num_threads(), "kind": "port",
-            "sample": f"{samples} full config-3 step(s) on the host: oracle/raster_oracle.c (OpenMP) rasterizer "
-                      "fwd/bwd + the reference's pure-torch propagation (python_function.py:35-78) on torch CPU + "
-                      "torch Adam"}
+            "sample": f"{warmup} warm-up + {samples} timed full config-3 step(s) (median) on the host: "
+                      "oracle/raster_oracle.c (OpenMP) rasterizer fwd/bwd + the reference's pure-torch propagation "
+                      "(python_function.py:35-78) on torch CPU + torch Adam",
+            "ms_per_step_samples": [round(t * 1e3, 1) for t in ts]}
 
 
 def ref_cuda_step_rate(steps, warmup):
@@ -424,14 +429,31 @@ def run_config4(args, world, rank, local):
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the config-3 step on the host cores (the reference's CPU path),
+    `--warmup` untimed steps then exactly `--steps` timed ones, with the same metric and
+    config as this build's line; the reference's CUDA kernels rebuilt for sm_100a are timed
+    beside it on this GPU."""
     if rank != 0:
         return None
-    base = cpu_baseline(samples=max(1, min(args.steps, 3)))
-    line = {"metric": METRIC, "value": base["value"], "unit": "iters/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 / base["value"], "higher_is_better": True,
+    from oracle.cpu_step import CpuHoloStep, num_threads
+    st = CpuHoloStep(N=N_GAUSS, W=IMG, H=IMG, K=K_PLANES)
+    for _ in range(args.warmup):
+        st.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        st.step()
+    ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    value = 1000.0 / ms
+    base = {"value": value, "unit": "iters/s", "cores": num_threads(), "kind": "port",
+            "sample": f"{args.warmup} warm-up + {args.steps} timed full config-3 steps on the host: "
+                      "oracle/raster_oracle.c (OpenMP) rasterizer fwd/bwd + the reference's pure-torch "
+                      "propagation (python_function.py:35-78) on torch CPU + torch Adam"}
+    line = {"metric": METRIC, "value": value, "unit": "iters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32/c64", "data": "synthetic (seeded, config-3 shapes)",
-            "config": dict(CONFIG, parallelism="host cpu"), "impl": "reference", "cpu_baseline": base,
-            "e2e": {"value": base["value"], "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": dict(CONFIG, parallelism=f"view-dp{world}" if world > 1 else "single"), "impl": "reference",
+            "execution": "host cpu (rank 0 only)", "cpu_baseline": base,
+            "e2e": {"value": value, "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if torch.cuda.is_available():
         try:
             line["reference_cuda_sm100a"] = ref_cuda_step_rate(max(min(args.steps, 20), 10), max(min(args.warmup, 5), 3))
@@ -652,7 +674,7 @@ def run_reference_component(args, world, rank):
                                 "sample": "1 forward: oracle/raster_oracle.c (OpenMP restatement of the "
                                           "reference rasterizer)"}
     line["impl"] = "reference"
-    line["config"]["parallelism"] = "host cpu"
+    line["execution"] = "host cpu (rank 0 only)"
     line["cpu_baseline"]["cores"] = threads
     line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     if torch.cuda.is_available():
@@ -723,7 +745,7 @@ def main():
         else:
             line = run_mine(args, world, rank, local)
             if line is not None and world == 1 and not args.no_cpu_baseline and args.workload == "config3":
-                line["cpu_baseline"] = cpu_baseline(samples=1)
+                line["cpu_baseline"] = cpu_baseline(samples=3, warmup=1)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

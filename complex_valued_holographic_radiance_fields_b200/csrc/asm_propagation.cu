@@ -163,7 +163,8 @@ __global__ void __launch_bounds__(512) asm_rows_inverse_kernel(
 using namespace cvhrf;
 
 struct cvhrf_asm_plan {
-  FftDesc desc;
+  FftDesc desc;     // the plan the kernels of this size run (compile-time radices where they exist)
+  FftDesc desc_rt;  // the runtime mixed-radix plan (its own digit-reversal table)
   void* dev_mem;
   int device;
 };
@@ -207,26 +208,34 @@ extern "C" int cvhrf_asm_plan_create(int S, cvhrf_asm_plan** plan_out) {
     double a = -2.0 * M_PI * (double)t / (double)P;
     twP[t] = make_float2((float)cos(a), (float)sin(a));
   }
-  // digit reversal: bin k = m1 + R1 (m2 + R2 (...)) sits at position sum_i L_i m_i, for the
-  // stage radices of the plan that will run (the compile-time plan where one exists)
-  int rad[kMaxFftStages], Ls[kMaxFftStages], nst = d.nst;
-  for (int i = 0; i < d.nst; ++i) { rad[i] = d.radix[i]; Ls[i] = d.L[i]; }
-  if (static_fft_size(S)) {
+  // digit reversal: bin k = m1 + R1 (m2 + R2 (...)) sits at position sum_i L_i m_i.  One table for
+  // the runtime radices of `d`, and, for a size with a compile-time plan, a second one for that
+  // plan's radices (the kernels of the two plans order their spectra differently).
+  auto digit_reversal = [S](const int* rad, const int* Ls, int nst) {
+    std::vector<int> dr(S);
+    for (int k = 0; k < S; ++k) {
+      int rem = k, pos = 0;
+      for (int i = 0; i < nst; ++i) {
+        int m = rem % rad[i];
+        rem /= rad[i];
+        pos += Ls[i] * m;
+      }
+      dr[pos] = k;
+    }
+    return dr;
+  };
+  std::vector<int> digrev_rt = digit_reversal(d.radix, d.L, d.nst);
+  std::vector<int> digrev_st = digrev_rt;
+  const bool has_static = static_fft_size(S);
+  if (has_static) {
+    int rad[kMaxFftStages], Ls[kMaxFftStages], nst = 0;
     static_fft_radices(S, rad, &nst);
     int L = S;
     for (int i = 0; i < nst; ++i) { L /= rad[i]; Ls[i] = L; }
+    digrev_st = digit_reversal(rad, Ls, nst);
   }
-  std::vector<int> digrev(S);
-  for (int k = 0; k < S; ++k) {
-    int rem = k, pos = 0;
-    for (int i = 0; i < nst; ++i) {
-      int m = rem % rad[i];
-      rem /= rad[i];
-      pos += Ls[i] * m;
-    }
-    digrev[pos] = k;
-  }
-  size_t bytes = (size_t)(S + P) * sizeof(float2) + (size_t)S * sizeof(int);
+  const size_t dr_off = (size_t)(S + P) * sizeof(float2);
+  size_t bytes = dr_off + 2 * (size_t)S * sizeof(int);
   cvhrf_asm_plan* plan = (cvhrf_asm_plan*)calloc(1, sizeof(cvhrf_asm_plan));
   if (!plan) return CVHRF_EINVAL;
   CVHRF_CUDA_TRY(cudaGetDevice(&plan->device));
@@ -235,11 +244,15 @@ extern "C" int cvhrf_asm_plan_create(int S, cvhrf_asm_plan** plan_out) {
   char* base = (char*)plan->dev_mem;
   e = cudaMemcpy(base, tw.data(), S * sizeof(float2), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMemcpy(base + S * sizeof(float2), twP.data(), P * sizeof(float2), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemcpy(base + (S + P) * sizeof(float2), digrev.data(), S * sizeof(int), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(base + dr_off, digrev_st.data(), S * sizeof(int), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(base + dr_off + S * sizeof(int), digrev_rt.data(), S * sizeof(int), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) { cudaFree(plan->dev_mem); free(plan); set_last_cuda_error((int)e); return CVHRF_ECUDA; }
   d.tw = (const float2*)base;
   d.twP = (const float2*)(base + S * sizeof(float2));
-  d.digrev = (const int*)(base + (S + P) * sizeof(float2));
+  d.digrev = (const int*)(base + dr_off);
+  plan->desc_rt = d;
+  plan->desc_rt.digrev = (const int*)(base + dr_off + S * sizeof(int));
   plan->desc = d;
   *plan_out = plan;
   return CVHRF_OK;
@@ -371,7 +384,9 @@ extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void
     if ((rc = static_columns(d, A, H, B, S, sj, C, st))) return rc;
     return static_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
   }
-  if ((rc = launch_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
+  // runtime plan: more planes per channel than the compile-time column pass sums
+  const FftDesc& dr = plan->desc_rt;
+  if ((rc = launch_rows_forward(dr, (const float2*)fields, K * C * H, W, A, st))) return rc;
   for (int p = 0; p < K; ++p) {
     ColumnJobs jobs{};
     jobs.n = C;
@@ -381,9 +396,9 @@ extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void
       jobs.out_item[c] = c;
       jobs.tp[c] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
     }
-    if ((rc = launch_columns(d, A, H, B, S, jobs, p > 0 ? 1 : 0, st))) return rc;
+    if ((rc = launch_columns(dr, A, H, B, S, jobs, p > 0 ? 1 : 0, st))) return rc;
   }
-  return launch_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+  return launch_rows_inverse(dr, B, C * S, (float2*)holo, S, 0, st);
 }
 
 extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, const void* grad_holo, int K, int C,

@@ -161,7 +161,9 @@ int cvhrf_asm_propagate_planes_adjoint_table(const cvhrf_asm_plan* plan,
  * result as cvhrf_asm_propagate otherwise.  The first call on a device looks up
  * that array's device address (with the device current); make that first call
  * before any stream capture.  All calls share the array and overwrite it, so calls
- * that overlap on the GPU race: order them on one stream.
+ * that overlap on the GPU race: order them on one stream.  The looked-up address is
+ * kept for the life of the process, so do not call it again on a device after
+ * cudaDeviceReset (or any other reset of that device's primary context).
  */
 int cvhrf_asm_propagate_noalloc(const void* in, int Hi, int Wi, void* out, int Ho, int Wo, int S,
                                 float wavelength, float pixel_pitch, float distance, float aperture,
@@ -518,8 +520,11 @@ int cvhrf_multiplane_loss_backward(const void* fields, int K, int C, int S, int 
  * is passed back to the backward, which writes grad_holo (torch's complex-gradient
  * convention; zero where h = 0) from grad_field.  The workspace
  * (cvhrf_hologram_field_workspace_bytes) is zeroed once with
- * cvhrf_hologram_field_init_workspace and left ready by every call; calls sharing it must
- * be ordered on one stream.  Reductions are in a fixed order (deterministic).
+ * cvhrf_hologram_field_init_workspace and left ready by every call.  The forward and the
+ * backward use the same completion counter and partial sums in it, so every call sharing
+ * one workspace (forward or backward, eager or inside a graph) must be ordered on one
+ * stream; concurrent users (two streams, two graphs replaying at once) each need their
+ * own workspace.  Reductions are in a fixed order (deterministic).
  */
 size_t cvhrf_hologram_field_workspace_bytes(void);
 int cvhrf_hologram_field_init_workspace(void* workspace, size_t workspace_bytes, void* stream);

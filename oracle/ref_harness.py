@@ -131,12 +131,42 @@ def get_rasterizer_info():
     return _last_info
 
 
+# Bytes of the reference rasterizer's image scratch buffer that its singleton pool holds.
+_img_buffer_held = 0
+
+
+def ref_image_buffer_bytes(W, H, K):
+    """The reference's image scratch request: required<ImageState>(num_tiles, H * W, K)
+    (rasterizer_splat.cu:483, rasterizer_splat.h:36-39) = tiles x pixels x K x
+    sizeof(ImageState) (three pointers) + 128 bytes."""
+    tiles = ((W + 15) // 16) * ((H + 15) // 16)
+    return tiles * W * H * K * 24 + 128
+
+
+def _guard_image_buffer(W, H, K, device):
+    """The reference prints and ignores a failed cudaMalloc of that buffer and then writes
+    through a null pointer (rasterizer_splat.cu:258-264).  Refuse, on the host, any call
+    whose buffer cannot be allocated (it is 387 GB at 1008 x 756 x 7 and 1.2 TB at
+    1920 x 1080 x 3)."""
+    global _img_buffer_held
+    need = ref_image_buffer_bytes(W, H, K)
+    if need <= _img_buffer_held:
+        return
+    torch.cuda.empty_cache()
+    free, _ = torch.cuda.mem_get_info(device)
+    if need + (4 << 30) > free + _img_buffer_held:
+        raise RuntimeError(f"reference rasterizer image scratch of {need / 2**30:.1f} GiB for {W}x{H}x{K} does not fit "
+                           f"({(free + _img_buffer_held) / 2**30:.1f} GiB available); not running the reference")
+    _img_buffer_held = need
+
+
 class RefSplatTileCuda(torch.autograd.Function):
     """python_import.py:283-342."""
 
     @staticmethod
     def forward(ctx, cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs,
                 fx, fy, px, py, view_matrix, img_size, near_plane, far_plane, tile_size=(16, 16)):
+        _guard_image_buffer(int(img_size[0]), int(img_size[1]), int(plane_probs.shape[1]), cam_means_3D.device)
         ctx.save_for_backward(cam_means_3D, z_vals, quats, scales, colours, phase, opacities, plane_probs, view_matrix)
         ctx.p = (fx, fy, px, py, img_size, tile_size, near_plane, far_plane)
         output, info = get_rasterizer().forward(cam_means_3D, z_vals, quats, scales, colours, phase, opacities,

@@ -34,6 +34,7 @@ class RefGpuHoloStep:
         loss = ((holo.abs() ** 2 - t.target) ** 2).mean()
         loss.backward()
         visible = idxs[vis]
+        self.last_visible = visible
         with torch.no_grad():
             for k, prm in t.params.items():
                 m, v = self.state[k]

@@ -66,7 +66,7 @@ def test_forward_vs_reference(cuda, ref, case):
     assert rel(field, rfield) < TOL
 
 
-@pytest.mark.parametrize("case", CASES[:5], ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
+@pytest.mark.parametrize("case", CASES, ids=lambda c: f"N{c['N']}_{c['W']}x{c['H']}_K{c['K']}_C{c['C']}")
 def test_backward_vs_reference(cuda, ref, case):
     kw = inputs(case["N"], case["W"], case["H"], case["K"], case["C"], seed=1)
     g = torch.Generator().manual_seed(5)
