@@ -53,6 +53,7 @@ SIGNATURES = {
     "cvhrf_inclusive_scan_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_inclusive_scan_u32": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "cvhrf_lookback_timeouts": (c_int, []),
+    "cvhrf_copy_wait_timeouts": (c_int, []),
     "cvhrf_intensity_loss_workspace_bytes": (c_size_t, [c_int]),
     "cvhrf_intensity_loss_init_workspace": (c_int, [c_void_p, c_size_t, c_void_p]),
     "cvhrf_intensity_loss": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),

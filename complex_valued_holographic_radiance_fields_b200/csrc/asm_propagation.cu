@@ -267,9 +267,12 @@ extern "C" int cvhrf_asm_plan_destroy(cvhrf_asm_plan* plan) {
 
 static const size_t kSmemBudget = 100 * 1024;
 
+// Both intermediates, sized for the transposed layout of the compile-time passes (column
+// stride col_stride(rows)); the runtime passes use the first rows x 2S values of each.
 static size_t ws_bytes_impl(int S, int in_items, int Hi, int out_items, int Ho) {
   const size_t P = 2 * (size_t)S;
-  return align_up((size_t)in_items * Hi * P * sizeof(float2), 256) + align_up((size_t)out_items * Ho * P * sizeof(float2), 256);
+  return align_up((size_t)in_items * col_stride(Hi) * P * sizeof(float2), 256) +
+         align_up((size_t)out_items * col_stride(Ho) * P * sizeof(float2), 256);
 }
 
 extern "C" size_t cvhrf_asm_workspace_bytes(int S, int items, int Hi, int Wi, int out_items, int Ho, int Wo) {
@@ -332,18 +335,22 @@ extern "C" int cvhrf_asm_propagate(const cvhrf_asm_plan* plan, const void* in, i
   if (!(wavelength > 0.0f) || !(pixel_pitch > 0.0f)) return CVHRF_EINVAL;
   Carver cv(workspace, workspace_bytes);
   const int P = 2 * d.S;
-  float2* A = cv.take<float2>((size_t)Hi * P);
-  float2* B = cv.take<float2>((size_t)Ho * P);
+  float2* A = cv.take<float2>((size_t)col_stride(Hi) * P);
+  float2* B = cv.take<float2>((size_t)col_stride(Ho) * P);
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
   if (static_fft_size(d.S)) {
-    SumJobs sj{};
-    sj.nin[0] = 1;
-    sj.tp[0][0] = make_transfer(wavelength, pixel_pitch, distance, aperture, P);
-    if ((rc = static_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
-    if ((rc = static_columns(d, A, Hi, B, Ho, sj, 1, st))) return rc;
-    return static_rows_inverse(d, B, Ho, (float2*)out, Wo, accumulate, st);
+    ColPlan cp;
+    cp.njobs = 1;
+    cp.item[0] = 0;
+    cp.n[0] = 1;
+    cp.items[0][0] = 0;
+    cp.tpi[0][0] = 0;
+    cp.tp[0] = make_transfer(wavelength, pixel_pitch, distance, aperture, P);
+    if ((rc = static_rows_forward(d, (const float2*)in, 1, Hi, Wi, A, st))) return rc;
+    if ((rc = static_columns(d, false, A, Hi, B, Ho, cp, nullptr, st))) return rc;
+    return static_rows_inverse(d, B, 1, Ho, (float2*)out, Wo, accumulate, st);
   }
   if ((rc = launch_rows_forward(d, (const float2*)in, Hi, Wi, A, st))) return rc;
   ColumnJobs jobs{};
@@ -364,25 +371,28 @@ extern "C" int cvhrf_asm_propagate_planes(const cvhrf_asm_plan* plan, const void
   if (K < 1 || C < 1 || K * C > kMaxJobs || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
   const int S = d.S, P = 2 * S;
   Carver cv(workspace, workspace_bytes);
-  float2* A = cv.take<float2>((size_t)K * C * H * P);
-  float2* B = cv.take<float2>((size_t)C * S * P);
+  float2* A = cv.take<float2>((size_t)K * C * col_stride(H) * P);
+  float2* B = cv.take<float2>((size_t)C * col_stride(S) * P);
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
-  if (static_fft_size(d.S) && K <= kMaxSumInputs) {
-    SumJobs sj{};
+  for (int c = 0; c < C; ++c)
+    if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+  if (static_fft_size(d.S) && K * C <= kMaxTableItems) {
+    ColPlan cp;
+    cp.njobs = C;
     for (int c = 0; c < C; ++c) {
-      if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
-      sj.nin[c] = K;
-      sj.out_item[c] = c;
+      cp.item[c] = c;
+      cp.n[c] = K;
       for (int p = 0; p < K; ++p) {
-        sj.in_item[c][p] = p * C + c;
-        sj.tp[c][p] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
+        cp.items[c][p] = (short)(p * C + c);
+        cp.tpi[c][p] = (short)(p * C + c);
+        cp.tp[p * C + c] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
       }
     }
-    if ((rc = static_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
-    if ((rc = static_columns(d, A, H, B, S, sj, C, st))) return rc;
-    return static_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+    if ((rc = static_rows_forward(d, (const float2*)fields, K * C, H, W, A, st))) return rc;
+    if ((rc = static_columns(d, false, A, H, B, S, cp, nullptr, st))) return rc;
+    return static_rows_inverse(d, B, C, S, (float2*)holo, S, 0, st);
   }
   // runtime plan: more planes per channel than the compile-time column pass sums
   const FftDesc& dr = plan->desc_rt;
@@ -410,24 +420,30 @@ extern "C" int cvhrf_asm_propagate_planes_adjoint(const cvhrf_asm_plan* plan, co
   if (K < 1 || C < 1 || K * C > kMaxJobs || !dims_ok(d.S, H, W)) return CVHRF_EINVAL;
   const int S = d.S, P = 2 * S;
   Carver cv(workspace, workspace_bytes);
-  float2* A = cv.take<float2>((size_t)C * S * P);
-  float2* B = cv.take<float2>((size_t)K * C * H * P);
+  float2* A = cv.take<float2>((size_t)C * col_stride(S) * P);
+  float2* B = cv.take<float2>((size_t)K * C * col_stride(H) * P);
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
   int rc;
-  if (static_fft_size(d.S)) {
-    SumJobs sj{};
-    for (int p = 0; p < K; ++p)
-      for (int c = 0; c < C; ++c) {
-        if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
-        sj.nin[p * C + c] = 1;
-        sj.out_item[p * C + c] = p * C + c;
-        sj.in_item[p * C + c][0] = c;
-        sj.tp[p * C + c][0] = make_transfer(wavelengths[c], pixel_pitch, -distances[p], aperture, P);
+  for (int c = 0; c < C; ++c)
+    if (!(wavelengths[c] > 0.0f)) return CVHRF_EINVAL;
+  if (static_fft_size(d.S) && K * C <= kMaxTableItems) {
+    ColPlan cp;
+    cp.njobs = C;
+    for (int c = 0; c < C; ++c) {
+      cp.item[c] = c;
+      cp.n[c] = K;
+      for (int p = 0; p < K; ++p) {
+        cp.items[c][p] = (short)(p * C + c);
+        cp.tpi[c][p] = (short)(p * C + c);
+        // the adjoint of propagation by d is propagation by -d: the scatter pass multiplies
+        // by conj(H_d) = H_-d, as it does with a table of H_d
+        cp.tp[p * C + c] = make_transfer(wavelengths[c], pixel_pitch, distances[p], aperture, P);
       }
-    if ((rc = static_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
-    if ((rc = static_columns(d, A, S, B, H, sj, K * C, st))) return rc;
-    return static_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+    }
+    if ((rc = static_rows_forward(d, (const float2*)grad_holo, C, S, S, A, st))) return rc;
+    if ((rc = static_columns(d, true, A, S, B, H, cp, nullptr, st))) return rc;
+    return static_rows_inverse(d, B, K * C, H, (float2*)grad_fields, W, 0, st);
   }
   if ((rc = launch_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
   ColumnJobs jobs{};
@@ -552,14 +568,21 @@ extern "C" int cvhrf_asm_propagate_planes_table(const cvhrf_asm_plan* plan, cons
   if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
   const int S = d.S, P = 2 * S;
   Carver cv(workspace, workspace_bytes);
-  float2* A = cv.take<float2>((size_t)K * C * H * P);
-  float2* B = cv.take<float2>((size_t)C * S * P);
+  float2* A = cv.take<float2>((size_t)K * C * col_stride(H) * P);
+  float2* B = cv.take<float2>((size_t)C * col_stride(S) * P);
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  ColPlan cp;
+  cp.njobs = C;
+  for (int c = 0; c < C; ++c) {
+    cp.item[c] = c;
+    cp.n[c] = K;
+    for (int p = 0; p < K; ++p) cp.items[c][p] = cp.tpi[c][p] = (short)(p * C + c);
+  }
   int rc;
-  if ((rc = static_rows_forward(d, (const float2*)fields, K * C * H, W, A, st))) return rc;
-  if ((rc = static_columns_table(d, false, A, H, B, S, (const float2*)table, K, C, st))) return rc;
-  return static_rows_inverse(d, B, C * S, (float2*)holo, S, 0, st);
+  if ((rc = static_rows_forward(d, (const float2*)fields, K * C, H, W, A, st))) return rc;
+  if ((rc = static_columns(d, false, A, H, B, S, cp, (const float2*)table, st))) return rc;
+  return static_rows_inverse(d, B, C, S, (float2*)holo, S, 0, st);
 }
 
 extern "C" int cvhrf_asm_propagate_planes_adjoint_table(const cvhrf_asm_plan* plan, const void* grad_holo, int K,
@@ -571,14 +594,21 @@ extern "C" int cvhrf_asm_propagate_planes_adjoint_table(const cvhrf_asm_plan* pl
   if (!static_fft_size(d.S)) return CVHRF_EUNSUPPORTED;
   const int S = d.S, P = 2 * S;
   Carver cv(workspace, workspace_bytes);
-  float2* A = cv.take<float2>((size_t)C * S * P);
-  float2* B = cv.take<float2>((size_t)K * C * H * P);
+  float2* A = cv.take<float2>((size_t)C * col_stride(S) * P);
+  float2* B = cv.take<float2>((size_t)K * C * col_stride(H) * P);
   if (cv.overflow || !workspace) return CVHRF_EWORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;
+  ColPlan cp;
+  cp.njobs = C;
+  for (int c = 0; c < C; ++c) {
+    cp.item[c] = c;
+    cp.n[c] = K;
+    for (int p = 0; p < K; ++p) cp.items[c][p] = cp.tpi[c][p] = (short)(p * C + c);
+  }
   int rc;
-  if ((rc = static_rows_forward(d, (const float2*)grad_holo, C * S, S, A, st))) return rc;
-  if ((rc = static_columns_table(d, true, A, S, B, H, (const float2*)table, K, C, st))) return rc;
-  return static_rows_inverse(d, B, K * C * H, (float2*)grad_fields, W, 0, st);
+  if ((rc = static_rows_forward(d, (const float2*)grad_holo, C, S, S, A, st))) return rc;
+  if ((rc = static_columns(d, true, A, S, B, H, cp, (const float2*)table, st))) return rc;
+  return static_rows_inverse(d, B, K * C, H, (float2*)grad_fields, W, 0, st);
 }
 
 extern "C" int cvhrf_asm_propagate_noalloc(const void* in, int Hi, int Wi, void* out, int Ho, int Wo, int S,

@@ -1,154 +1,375 @@
-// Propagation passes specialised for compile-time line lengths (see fft_static.cuh).
+// Propagation passes specialised for compile-time line lengths (S = 64 ... 2048).
 //
-// Same three-pass algorithm and arithmetic as asm_propagation.cu (rows forward; columns
-// with the transfer function; rows inverse with crop), with two differences:
-//   * the FFTs use StaticPlan<S> (composite radices <= 32 in registers);
-//   * the column pass sums several inputs (the K planes of one channel, each with its own
-//     transfer function) into one output in shared memory, so a multi-plane propagation
-//     writes the intermediate once instead of read-modify-writing it per plane.
+// The operator and its arithmetic are those of asm_propagation.cu: rows forward; columns
+// with the band-limited transfer function; rows inverse with the crop.  The layout and
+// the work split are built for the B200 memory system:
+//
+//   * The intermediate spectra are stored TRANSPOSED (item, column q, row): the row pass
+//     writes each column's rows as 32- or 64-byte runs, the column pass reads and writes
+//     whole contiguous columns, and the inverse row pass reads the runs back.  Every DRAM
+//     sector moved carries only useful bytes.
+//   * The column pass stages its columns with bulk asynchronous copies (TMA
+//     cp.async.bulk, completion on an mbarrier): one thread issues a block's whole
+//     column group for the next plane while the warps transform the current one.
+//   * Every transform line belongs to one warp from its first FFT stage to its last
+//     (fft_warp.cuh), so FFT stages are separated by __syncwarp(), not block barriers;
+//     a block synchronises only where its warps hand data to one another (staging
+//     buffer, transposed stores).
+//   * The K planes of a channel are summed in the spectrum (the inverse transform is
+//     linear): a column costs K forward transforms and one inverse; the adjoint costs one
+//     forward and K inverse transforms.  The transfer function is evaluated in the pass
+//     (per-column terms hoisted) or read from a precomputed table.
 #include "asm_static.cuh"
-#include "fft_static.cuh"
+#include "fft_warp.cuh"
+
+namespace cvhrf {
+
+__device__ int g_copy_wait_timeouts;
+
+namespace {
+
+constexpr long kMaxPolls = 1L << 24;
+
+// Bounded wait on a bulk-copy mbarrier phase; on give-up it counts a timeout (the result
+// of that launch is then invalid) and returns false.
+__device__ __forceinline__ bool wait_copies(uint64_t* bar, unsigned parity) {
+  for (long i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  atomicAdd(&g_copy_wait_timeouts, 1);
+  return false;
+}
+
+}  // namespace
+}  // namespace cvhrf
+
+#include "asm_fourstep.cuh"
 
 namespace cvhrf {
 namespace {
 
-constexpr int kThreads = 256;
-
+// Work split per line length (the warp-line passes: sizes other than 800 and 1024).
 template <int S>
-__global__ void __launch_bounds__(kThreads) rows_forward_s(const float2* __restrict__ in, int total_rows, int Wi,
-                                                          float2* __restrict__ A, const float2* __restrict__ tw,
-                                                          const float2* __restrict__ twP, int rows) {
-  extern __shared__ float2 sm[];
-  constexpr int P = 2 * S;
+struct Split {
+  static constexpr int RPW = S >= 800 ? 1 : (S >= 256 ? 2 : 4);  // rows per warp (row passes)
+  static constexpr int NWR = S >= 1024 ? 4 : 8;                  // warps per block (row passes)
+  static constexpr int ROWS = RPW * NWR;                         // rows per block (row passes)
+  static constexpr int LPW = S >= 800 ? 1 : (S >= 256 ? 2 : 4);  // lines per warp (column passes)
+  static constexpr int COLS = S == 800 ? 3 : (S == 1024 ? 2 : (S > 1024 ? 1 : 4));  // columns per block
+  static constexpr int NWC = 2 * COLS / LPW;                     // warps per block (column passes)
+  static constexpr int LD = line_ld(S);
+};
+
+// ---- pass A: rows forward, transposed store ------------------------------------------
+template <int S>
+__global__ void __launch_bounds__(Split<S>::NWR * 32) rows_fwd_t(const float2* __restrict__ in, int items, int Hi,
+                                                                int Wi, float2* __restrict__ A,
+                                                                const float2* __restrict__ tw,
+                                                                const float2* __restrict__ twP) {
+  using SP = Split<S>;
+  constexpr int P = 2 * S, LD = SP::LD, ROWS = SP::ROWS, NT = SP::NWR * 32;
+  extern __shared__ __align__(16) float2 sm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int total = items * Hi;
+  const int row0 = blockIdx.x * ROWS;
   const int ow = (P - Wi) / 2;
-  const int row0 = blockIdx.x * rows;
-  const int nrows = min(rows, total_rows - row0);
-  if (nrows <= 0) return;
-  // all of the block's row loads in flight at once (asynchronous copies), then the odd
-  // half-lines are formed in place
-  for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
-    const int r = e / S, t = e - r * S;
-    int j = t - ow;
-    if (j < 0 || j >= Wi) j = t + S - ow;
-    float2* dst = sm + (2 * r) * S + t;
-    if (j >= 0 && j < Wi) cp_async8(dst, in + (size_t)(row0 + r) * Wi + j);
-    else *dst = make_float2(0.f, 0.f);
+  // each warp loads and folds its rows: line 2r holds x[n] at n mod S, line 2r + 1 holds
+  // x[n] w_2S^n (the odd output bins).  The loads are asynchronous copies, all in flight
+  // at once; the odd lines are formed once they land.
+  for (int rr = 0; rr < SP::RPW; ++rr) {
+    const int r = warp * SP::RPW + rr;
+    const int g = row0 + r;
+    float2* le = sm + (2 * r) * LD;
+    const float2* src = in + (size_t)(g < total ? g : 0) * Wi;
+    for (int t = lane; t < S; t += 32) {
+      int j = t - ow;
+      if (j < 0 || j >= Wi) j = t + S - ow;
+      if (g < total && j >= 0 && j < Wi) cp_async8(le + pidx(t), src + j);
+      else le[pidx(t)] = make_float2(0.f, 0.f);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait_all();
+  __syncwarp();
+  for (int rr = 0; rr < SP::RPW; ++rr) {
+    const int r = warp * SP::RPW + rr;
+    const float2* le = sm + (2 * r) * LD;
+    float2* lo = sm + (2 * r + 1) * LD;
+    for (int t = lane; t < S; t += 32) {
+      const int j = t - ow;
+      const int pos = (j < 0 || j >= Wi) ? t + S : t;
+      lo[pidx(t)] = pmul(le[pidx(t)], __ldg(&twP[pos]));
+    }
+  }
+  __syncwarp();
+  warp_fft_forward<S>(sm + (2 * warp * SP::RPW) * LD, 2 * SP::RPW, lane, tw);
+  __syncthreads();
+  // transposed store: for every spectrum column q, the block's ROWS rows are one run
+  const int HiS = col_stride(Hi);
+  for (int e = threadIdx.x; e < ROWS * P; e += NT) {
+    const int q = e / ROWS, r = e - q * ROWS;
+    const int g = row0 + r;
+    if (g >= total) continue;
+    const int item = g / Hi, rr = g - item * Hi;
+    const int h = q >= S ? 1 : 0;
+    A[((size_t)item * P + q) * HiS + rr] = sm[(2 * r + h) * LD + pidx(q - h * S)];
+  }
+}
+
+// ---- pass C: rows inverse from the transposed spectra, crop, scale -------------------
+template <int S>
+__global__ void __launch_bounds__(Split<S>::NWR * 32) rows_inv_t(const float2* __restrict__ B, int items, int Ho,
+                                                                float2* __restrict__ out, int Wo,
+                                                                const float2* __restrict__ tw,
+                                                                const float2* __restrict__ twP, float scale,
+                                                                int accumulate) {
+  using SP = Split<S>;
+  constexpr int P = 2 * S, LD = SP::LD, ROWS = SP::ROWS, NT = SP::NWR * 32;
+  extern __shared__ __align__(16) float2 sm[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int total = items * Ho;
+  const int row0 = blockIdx.x * ROWS;
+  const int HoS = col_stride(Ho);
+  for (int e = threadIdx.x; e < ROWS * P; e += NT) {
+    const int q = e / ROWS, r = e - q * ROWS;
+    const int g = row0 + r;
+    const int h = q >= S ? 1 : 0;
+    float2* dst = sm + (2 * r + h) * LD + pidx(q - h * S);
+    if (g < total) {
+      const int item = g / Ho, rr = g - item * Ho;
+      cp_async8(dst, B + ((size_t)item * P + q) * HoS + rr);
+    } else {
+      *dst = make_float2(0.f, 0.f);
+    }
   }
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
-  for (int e = threadIdx.x; e < nrows * S; e += blockDim.x) {
-    const int r = e / S, t = e - r * S;
-    const int j = t - ow;
-    const int pos = (j < 0 || j >= Wi) ? t + S : t;
-    sm[(2 * r + 1) * S + t] = cmul(sm[(2 * r) * S + t], __ldg(&twP[pos]));
-  }
-  __syncthreads();
-  static_fft_forward<S>(sm, 2 * nrows, S, tw);
-  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
-    const int r = e / P, q = e - r * P;
-    A[(size_t)(row0 + r) * P + q] = sm[(2 * r) * S + q];
+  warp_fft_inverse<S>(sm + (2 * warp * SP::RPW) * LD, 2 * SP::RPW, lane, tw);
+  const int oc = (P - Wo) / 2;
+  for (int rr = 0; rr < SP::RPW; ++rr) {
+    const int r = warp * SP::RPW + rr;
+    const int g = row0 + r;
+    if (g >= total) break;
+    const float2* le = sm + (2 * r) * LD;
+    const float2* lo = le + LD;
+    float2* dst = out + (size_t)g * Wo;
+    for (int x = lane; x < Wo; x += 32) {
+      const int n = oc + x;
+      const int t = n >= S ? n - S : n;
+      float2 v = padd(le[pidx(t)], pmul(cconj(__ldg(&twP[n])), lo[pidx(t)]));
+      v.x *= scale;
+      v.y *= scale;
+      if (accumulate) v = padd(dst[x], v);
+      dst[x] = v;
+    }
   }
 }
 
+// Fill this warp's lines (line gl = 2 cc + h of the block) from the staged columns:
+// the even half-line takes the column, the odd one the column times w_2S^n.
 template <int S>
-__global__ void __launch_bounds__(kThreads) columns_s(const float2* __restrict__ A, int Hi, float2* __restrict__ B,
-                                                     int Ho, const float2* __restrict__ tw,
-                                                     const float2* __restrict__ twP, const int* __restrict__ digrev,
-                                                     int cols, const SumJobs jobs) {
-  extern __shared__ float2 sm[];
-  constexpr int P = 2 * S;
-  constexpr int LD = S + 1;  // padded line stride: consecutive lines start in different banks
-  const int job = blockIdx.y;
-  const int q0 = blockIdx.x * cols;
-  const int ncols = min(cols, P - q0);
-  float2* acc = sm + 2 * cols * LD;  // Ho x ncols output accumulator
-  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
-  const int nin = jobs.nin[job];
-  for (int k = 0; k < nin; ++k) {
-    const float2* Ain = A + (size_t)jobs.in_item[job][k] * Hi * P;
-    const TransferParams tp = jobs.tp[job][k];
+__device__ __forceinline__ void fold_columns(float2* lines, int gl0, int nl, const float2* stage, int HiS, int Hi,
+                                             int lane, const float2* __restrict__ twP) {
+  constexpr int P = 2 * S, LD = line_ld(S);
+  const int oh = (P - Hi) / 2;
+  for (int l = 0; l < nl; ++l) {
+    const int gl = gl0 + l, cc = gl >> 1, h = gl & 1;
+    const float2* col = stage + cc * HiS;
+    float2* line = lines + l * LD;
 #pragma unroll 4
-    for (int e = threadIdx.x; e < ncols * S; e += blockDim.x) {
-      const int t = e / ncols, c = e - t * ncols;
-      int pos = t;
-      int r = pos - oh;
-      if (r < 0 || r >= Hi) { pos = t + S; r = pos - oh; }
-      float2 v = make_float2(0.f, 0.f), vo = v;
-      if (r >= 0 && r < Hi) {
-        v = Ain[(size_t)r * P + q0 + c];
-        vo = cmul(v, __ldg(&twP[pos]));
-      }
-      sm[(2 * c) * LD + t] = v;
-      sm[(2 * c + 1) * LD + t] = vo;
+    for (int t = lane; t < S; t += 32) {
+      int r = t - oh, pos = t;
+      if (r < 0 || r >= Hi) { r = t + S - oh; pos = t + S; }
+      float2 v = make_float2(0.f, 0.f);
+      if (r >= 0 && r < Hi) v = col[r];
+      line[pidx(t)] = h ? pmul(v, __ldg(&twP[pos])) : v;
     }
-    __syncthreads();
-    static_fft_forward<S>(sm, 2 * ncols, LD, tw);
-    for (int e = threadIdx.x; e < 2 * ncols * S; e += blockDim.x) {
-      const int line = e / S, pos = e - line * S;
-      const int c = line >> 1, h = line & 1;
-      const int q = q0 + c;
-      const int qh = q >= S ? 1 : 0;
-      const int kv = 2 * __ldg(&digrev[q - qh * S]) + qh;
-      const int ku = 2 * __ldg(&digrev[pos]) + h;
-      sm[line * LD + pos] = cmul(sm[line * LD + pos], transfer_at(ku, kv, P, tp));
+  }
+  __syncwarp();
+}
+
+// ---- pass B, sum form: out[job] = sum_k P_k(in[k]) per column ------------------------
+// Shared memory: staging (COLS x col_stride(Hi) values, bulk-copy target), then 2 COLS
+// work lines and 2 COLS spectrum lines.
+template <int S, bool TABLE>
+__global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_sum_t(const float2* __restrict__ A, int Hi,
+                                                                float2* __restrict__ B, int Ho, const ColPlan plan,
+                                                                const float2* __restrict__ table,
+                                                                const float2* __restrict__ tw,
+                                                                const float2* __restrict__ twP,
+                                                                const int* __restrict__ digrev) {
+  using SP = Split<S>;
+  constexpr int P = 2 * S, LD = SP::LD, COLS = SP::COLS, LPW = SP::LPW, NT = SP::NWC * 32;
+  extern __shared__ __align__(16) float2 sm[];
+  __shared__ uint64_t bar;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int job = blockIdx.y;
+  const int q0 = blockIdx.x * COLS;
+  const int ncols = min(COLS, P - q0);
+  const int HiS = col_stride(Hi), HoS = col_stride(Ho);
+  float2* stage = sm;
+  float2* work = sm + ((COLS * HiS + 1) & ~1);
+  float2* spec = work + 2 * COLS * LD;
+  const int gl0 = warp * LPW;
+  const int nl = max(0, min(LPW, 2 * ncols - gl0));
+  float2* wl = work + gl0 * LD;
+  float2* sl = spec + gl0 * LD;
+  const int nin = plan.n[job];
+  const unsigned bytes = (unsigned)(ncols * HiS * sizeof(float2));
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  auto issue = [&](int k) {
+    const float2* src = A + ((size_t)plan.items[job][k] * P + q0) * HiS;
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_copy_g2s(stage, src, bytes, &bar);
+  };
+  if (threadIdx.x == 0) issue(0);
+  // per-line column terms of the transfer function (the column bin is fixed per line)
+  int kv[LPW];
+#pragma unroll
+  for (int l = 0; l < LPW; ++l) {
+    int q = q0 + ((gl0 + l) >> 1);
+    q = q < P ? q : 0;
+    const int qh = q >= S ? 1 : 0;
+    kv[l] = 2 * __ldg(&digrev[q - qh * S]) + qh;
+  }
+  for (int k = 0; k < nin; ++k) {
+    wait_copies(&bar, k & 1);
+    fold_columns<S>(wl, gl0, nl, stage, HiS, Hi, lane, twP);
+    __syncthreads();                       // every warp is done with the staging buffer
+    if (threadIdx.x == 0 && k + 1 < nin) {
+      fence_proxy_async_smem();
+      issue(k + 1);
     }
+    warp_fft_forward_head<S>(wl, nl, lane, tw);
+    const int ti = plan.tpi[job][k];
+    if constexpr (TABLE) {
+      const float2* Hb = table + (size_t)ti * P * P;
+      warp_last_forward_mul_acc<S>(wl, sl, nl, lane, k == 0, [&](int l, int pos) {
+        const int gl = gl0 + l;
+        return __ldg(&Hb[((size_t)(q0 + (gl >> 1)) * 2 + (gl & 1)) * S + pos]);
+      });
+    } else {
+      const TransferParams tp = plan.tp[ti];
+      TransferCol col[LPW];
+#pragma unroll
+      for (int l = 0; l < LPW; ++l) col[l] = transfer_col(kv[l], P, tp);
+      warp_last_forward_mul_acc<S>(wl, sl, nl, lane, k == 0, [&](int l, int pos) {
+        const int ku = 2 * __ldg(&digrev[pos]) + ((gl0 + l) & 1);
+        TransferCol c = col[0];
+#pragma unroll
+        for (int i = 1; i < LPW; ++i)
+          if (l == i) c = col[i];
+        return transfer_row(ku, P, c, tp);
+      });
+    }
+  }
+  warp_fft_inverse<S>(sl, nl, lane, tw);
+  __syncthreads();
+  // crop and fold back: y[n] = e[n mod S] + w_2S^-n o[n mod S]; each column is one run
+  const int oc = (P - Ho) / 2;
+  float2* Bout = B + ((size_t)plan.item[job] * P + q0) * HoS;
+  for (int e = threadIdx.x; e < ncols * Ho; e += NT) {
+    const int cc = e / Ho, rr = e - cc * Ho;
+    const int n = oc + rr;
+    const int t = n >= S ? n - S : n;
+    const float2* se = spec + (2 * cc) * LD;
+    Bout[(size_t)cc * HoS + rr] = padd(se[pidx(t)], pmul(cconj(__ldg(&twP[n])), se[LD + pidx(t)]));
+  }
+}
+
+// ---- pass B, scatter form: out[items[k]] = P_k(in) per column ------------------------
+template <int S, bool TABLE>
+__global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_scatter_t(const float2* __restrict__ A, int Hi,
+                                                                    float2* __restrict__ B, int Ho,
+                                                                    const ColPlan plan,
+                                                                    const float2* __restrict__ table,
+                                                                    const float2* __restrict__ tw,
+                                                                    const float2* __restrict__ twP,
+                                                                    const int* __restrict__ digrev) {
+  using SP = Split<S>;
+  constexpr int P = 2 * S, LD = SP::LD, COLS = SP::COLS, LPW = SP::LPW, NT = SP::NWC * 32;
+  extern __shared__ __align__(16) float2 sm[];
+  __shared__ uint64_t bar;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int job = blockIdx.y;
+  const int q0 = blockIdx.x * COLS;
+  const int ncols = min(COLS, P - q0);
+  const int HiS = col_stride(Hi), HoS = col_stride(Ho);
+  float2* stage = sm;
+  float2* work = sm + ((COLS * HiS + 1) & ~1);
+  float2* spec = work + 2 * COLS * LD;
+  const int gl0 = warp * LPW;
+  const int nl = max(0, min(LPW, 2 * ncols - gl0));
+  float2* wl = work + gl0 * LD;
+  float2* sl = spec + gl0 * LD;
+  const unsigned bytes = (unsigned)(ncols * HiS * sizeof(float2));
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_copy_g2s(stage, A + ((size_t)plan.item[job] * P + q0) * HiS, bytes, &bar);
+  }
+  int kv[LPW];
+#pragma unroll
+  for (int l = 0; l < LPW; ++l) {
+    int q = q0 + ((gl0 + l) >> 1);
+    q = q < P ? q : 0;
+    const int qh = q >= S ? 1 : 0;
+    kv[l] = 2 * __ldg(&digrev[q - qh * S]) + qh;
+  }
+  wait_copies(&bar, 0);
+  fold_columns<S>(sl, gl0, nl, stage, HiS, Hi, lane, twP);
+  warp_fft_forward<S>(sl, nl, lane, tw);
+  const int oc = (P - Ho) / 2;
+  const int nout = plan.n[job];
+  for (int k = 0; k < nout; ++k) {
+    const int ti = plan.tpi[job][k];
+    if constexpr (TABLE) {
+      const float2* Hb = table + (size_t)ti * P * P;
+      warp_first_inverse_mul<S>(sl, wl, nl, lane, [&](int l, int pos) {
+        const int gl = gl0 + l;
+        return __ldg(&Hb[((size_t)(q0 + (gl >> 1)) * 2 + (gl & 1)) * S + pos]);
+      });
+    } else {
+      const TransferParams tp = plan.tp[ti];
+      TransferCol col[LPW];
+#pragma unroll
+      for (int l = 0; l < LPW; ++l) col[l] = transfer_col(kv[l], P, tp);
+      warp_first_inverse_mul<S>(sl, wl, nl, lane, [&](int l, int pos) {
+        const int ku = 2 * __ldg(&digrev[pos]) + ((gl0 + l) & 1);
+        TransferCol c = col[0];
+#pragma unroll
+        for (int i = 1; i < LPW; ++i)
+          if (l == i) c = col[i];
+        return transfer_row(ku, P, c, tp);
+      });
+    }
+    warp_fft_inverse_rest<S>(wl, nl, lane, tw);
     __syncthreads();
-    static_fft_inverse<S>(sm, 2 * ncols, LD, tw);
-    for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
-      const int rr = e / ncols, c = e - rr * ncols;
+    float2* Bout = B + ((size_t)plan.items[job][k] * P + q0) * HoS;
+    for (int e = threadIdx.x; e < ncols * Ho; e += NT) {
+      const int cc = e / Ho, rr = e - cc * Ho;
       const int n = oc + rr;
       const int t = n >= S ? n - S : n;
-      const float2 v = cadd(sm[(2 * c) * LD + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * c + 1) * LD + t]));
-      acc[e] = k == 0 ? v : cadd(acc[e], v);
+      const float2* we = work + (2 * cc) * LD;
+      Bout[(size_t)cc * HoS + rr] = padd(we[pidx(t)], pmul(cconj(__ldg(&twP[n])), we[LD + pidx(t)]));
     }
-    __syncthreads();
-  }
-  float2* Bout = B + (size_t)jobs.out_item[job] * Ho * P;
-  for (int e = threadIdx.x; e < Ho * ncols; e += blockDim.x) {
-    const int rr = e / ncols, c = e - rr * ncols;
-    Bout[(size_t)rr * P + q0 + c] = acc[e];
-  }
-}
-
-template <int S>
-__global__ void __launch_bounds__(kThreads) rows_inverse_s(const float2* __restrict__ B, int total_rows,
-                                                          float2* __restrict__ out, int Wo,
-                                                          const float2* __restrict__ tw,
-                                                          const float2* __restrict__ twP, int rows, float scale,
-                                                          int accumulate) {
-  extern __shared__ float2 sm[];
-  constexpr int P = 2 * S;
-  const int row0 = blockIdx.x * rows;
-  const int nrows = min(rows, total_rows - row0);
-  if (nrows <= 0) return;
-  for (int e = threadIdx.x; e < nrows * P; e += blockDim.x) {
-    const int r = e / P, q = e - r * P;
-    cp_async8(sm + (2 * r) * S + q, B + (size_t)(row0 + r) * P + q);
-  }
-  cp_async_commit();
-  cp_async_wait_all();
-  __syncthreads();
-  static_fft_inverse<S>(sm, 2 * nrows, S, tw);
-  const int oc = (P - Wo) / 2;
-  for (int e = threadIdx.x; e < nrows * Wo; e += blockDim.x) {
-    const int r = e / Wo, x = e - r * Wo;
-    const int n = oc + x;
-    const int t = n >= S ? n - S : n;
-    float2 v = cadd(sm[(2 * r) * S + t], cmul(cconj(__ldg(&twP[n])), sm[(2 * r + 1) * S + t]));
-    v.x *= scale;
-    v.y *= scale;
-    float2* dst = out + (size_t)(row0 + r) * Wo + x;
-    if (accumulate) v = cadd(*dst, v);
-    *dst = v;
+    __syncthreads();                       // the work lines are rewritten by the next output
   }
 }
 
 // Transfer table of one input item: H[(q * 2 + h) * S + pos] = transfer x aperture at row
 // bin ku = 2 digrev[pos] + h and column bin kv of column q (the column pass layout).
 template <int S>
-__global__ void __launch_bounds__(kThreads) transfer_table_s(float2* __restrict__ table, const int* __restrict__ digrev,
-                                                            const TransferTable tt) {
+__global__ void __launch_bounds__(256) transfer_table_s(float2* __restrict__ table, const int* __restrict__ digrev,
+                                                        const TransferTable tt) {
   constexpr int P = 2 * S;
   const int item = blockIdx.y;
   const TransferParams tp = tt.tp[item];
@@ -167,8 +388,8 @@ __global__ void __launch_bounds__(kThreads) transfer_table_s(float2* __restrict_
 // Hc[item][y][x] at row bin (y + S) mod P and column bin (x + S) mod P, reordered into the
 // column pass layout of transfer_table_s.
 template <int S>
-__global__ void __launch_bounds__(kThreads) transfer_upload_s(float2* __restrict__ table, const int* __restrict__ digrev,
-                                                             const float2* __restrict__ Hc) {
+__global__ void __launch_bounds__(256) transfer_upload_s(float2* __restrict__ table, const int* __restrict__ digrev,
+                                                         const float2* __restrict__ Hc) {
   constexpr int P = 2 * S;
   const int item = blockIdx.y;
   float2* H = table + (size_t)item * P * P;
@@ -184,175 +405,65 @@ __global__ void __launch_bounds__(kThreads) transfer_upload_s(float2* __restrict
   }
 }
 
-// Column pass of a K-plane propagation with a precomputed transfer table: for channel c
-// = blockIdx.y, sum over planes p of H[p, c] * FFT(column of A[p * C + c]) is accumulated
-// in shared memory and inverse-transformed once (the inverse transform is linear), so a
-// column costs K forward transforms and one inverse.  The columns of plane p + 1 are
-// fetched with asynchronous copies into a staging line while plane p is transformed.
-// Shared memory: 2 COLS work lines, 2 COLS spectrum lines, COLS staging lines (stride S+1).
-template <int S, int COLS, int NT>
-__global__ void __launch_bounds__(NT) columns_sum_table_s(const float2* __restrict__ A, int Hi,
-                                                         float2* __restrict__ B, int Ho,
-                                                         const float2* __restrict__ tw,
-                                                         const float2* __restrict__ twP,
-                                                         const float2* __restrict__ table, int K, int C) {
-  extern __shared__ float2 sm[];
-  constexpr int P = 2 * S;
-  constexpr int LD = S + 1;
-  float2* work = sm;
-  float2* spec = sm + 2 * COLS * LD;
-  float2* raw = sm + 4 * COLS * LD;
-  const int c = blockIdx.y;
-  const int q0 = blockIdx.x * COLS;
-  const int ncols = min(COLS, P - q0);
-  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
-  auto fetch = [&](int p) {
-    const float2* Ain = A + (size_t)(p * C + c) * Hi * P + q0;
-    for (int e = threadIdx.x; e < ncols * S; e += NT) {
-      const int t = e / ncols, cc = e - t * ncols;
-      int r = t - oh;
-      if (r < 0 || r >= Hi) r = t + S - oh;
-      float2* dst = raw + cc * LD + t;
-      if (r >= 0 && r < Hi) cp_async8(dst, Ain + (size_t)r * P + cc);
-      else *dst = make_float2(0.f, 0.f);
-    }
-    cp_async_commit();
-  };
-  fetch(0);
-  for (int p = 0; p < K; ++p) {
-    cp_async_wait_all();
-    __syncthreads();
-    for (int e = threadIdx.x; e < ncols * S; e += NT) {
-      const int cc = e / S, t = e - cc * S;
-      const int r = t - oh;
-      const int pos = (r < 0 || r >= Hi) ? t + S : t;
-      const float2 v = raw[cc * LD + t];
-      work[(2 * cc) * LD + t] = v;
-      work[(2 * cc + 1) * LD + t] = cmul(v, __ldg(&twP[pos]));
-    }
-    __syncthreads();
-    if (p + 1 < K) fetch(p + 1);
-    static_fft_forward_head<S>(work, 2 * ncols, LD, tw);
-    static_last_forward_mul_acc<S>(work, spec, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0, p == 0);
-  }
-  __syncthreads();
-  static_fft_inverse<S>(spec, 2 * ncols, LD, tw);
-  float2* Bout = B + (size_t)c * Ho * P;
-  for (int e = threadIdx.x; e < Ho * ncols; e += NT) {
-    const int rr = e / ncols, cc = e - rr * ncols;
-    const int n = oc + rr;
-    const int t = n >= S ? n - S : n;
-    Bout[(size_t)rr * P + q0 + cc] = cadd(spec[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), spec[(2 * cc + 1) * LD + t]));
-  }
-}
-
-// Adjoint column pass with the same table: the column of A[c] is transformed once, then
-// for every plane p the spectrum times conj(H[p, c]) (the transfer function of distance
-// -d_p) is inverse-transformed, cropped and written to B[p * C + c].
-// Shared memory: 2 COLS spectrum lines and 2 COLS work lines (stride S+1).
-template <int S, int COLS, int NT>
-__global__ void __launch_bounds__(NT) columns_scatter_table_s(const float2* __restrict__ A, int Hi,
-                                                             float2* __restrict__ B, int Ho,
-                                                             const float2* __restrict__ tw,
-                                                             const float2* __restrict__ twP,
-                                                             const float2* __restrict__ table, int K, int C) {
-  extern __shared__ float2 sm[];
-  constexpr int P = 2 * S;
-  constexpr int LD = S + 1;
-  float2* work = sm;
-  float2* spec = sm + 2 * COLS * LD;
-  const int c = blockIdx.y;
-  const int q0 = blockIdx.x * COLS;
-  const int ncols = min(COLS, P - q0);
-  const int oh = (P - Hi) / 2, oc = (P - Ho) / 2;
-  const float2* Ain = A + (size_t)c * Hi * P + q0;
-  for (int e = threadIdx.x; e < ncols * S; e += NT) {
-    const int t = e / ncols, cc = e - t * ncols;
-    int r = t - oh;
-    if (r < 0 || r >= Hi) r = t + S - oh;
-    float2* dst = spec + (2 * cc) * LD + t;
-    if (r >= 0 && r < Hi) cp_async8(dst, Ain + (size_t)r * P + cc);
-    else *dst = make_float2(0.f, 0.f);
-  }
-  cp_async_commit();
-  cp_async_wait_all();
-  __syncthreads();
-  for (int e = threadIdx.x; e < ncols * S; e += NT) {
-    const int cc = e / S, t = e - cc * S;
-    const int r = t - oh;
-    const int pos = (r < 0 || r >= Hi) ? t + S : t;
-    spec[(2 * cc + 1) * LD + t] = cmul(spec[(2 * cc) * LD + t], __ldg(&twP[pos]));
-  }
-  __syncthreads();
-  static_fft_forward<S>(spec, 2 * ncols, LD, tw);
-  for (int p = 0; p < K; ++p) {
-    static_first_inverse_mul<S>(spec, work, 2 * ncols, LD, table + (size_t)(p * C + c) * P * P, q0);
-    __syncthreads();
-    static_fft_inverse_rest<S>(work, 2 * ncols, LD, tw);
-    float2* Bout = B + (size_t)(p * C + c) * Ho * P;
-    for (int e = threadIdx.x; e < Ho * ncols; e += NT) {
-      const int rr = e / ncols, cc = e - rr * ncols;
-      const int n = oc + rr;
-      const int t = n >= S ? n - S : n;
-      Bout[(size_t)rr * P + q0 + cc] = cadd(work[(2 * cc) * LD + t], cmul(cconj(__ldg(&twP[n])), work[(2 * cc + 1) * LD + t]));
-    }
-    __syncthreads();
-  }
-}
-
-constexpr size_t kStaticSmem = 64 * 1024;
-
 template <int S>
-int static_lines(size_t extra_per_line, size_t budget = kStaticSmem) {
-  const size_t per = 2 * (size_t)S * sizeof(float2) + extra_per_line;
-  int r = (int)(budget / per);
-  int p2 = 1;
-  while (p2 * 2 <= r && p2 < 8) p2 *= 2;
-  return p2;
+size_t row_smem() {
+  return (size_t)Split<S>::ROWS * 2 * Split<S>::LD * sizeof(float2);
+}
+template <int S>
+size_t col_smem(int Hi) {
+  using SP = Split<S>;
+  return (size_t)((SP::COLS * col_stride(Hi) + 1) & ~1) * sizeof(float2) + (size_t)4 * SP::COLS * SP::LD * sizeof(float2);
 }
 
 template <int S>
-int run_rows_forward(const float2* in, int total_rows, int Wi, float2* A, const float2* tw, const float2* twP,
+int run_rows_forward(const float2* in, int items, int Hi, int Wi, float2* A, const float2* tw, const float2* twP,
                      cudaStream_t st) {
-  const int rows = static_lines<S>(0);
-  const size_t smem = (size_t)rows * 2 * S * sizeof(float2);
-  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_forward_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  rows_forward_s<S><<<(total_rows + rows - 1) / rows, kThreads, smem, st>>>(in, total_rows, Wi, A, tw, twP, rows);
+  using SP = Split<S>;
+  const int total = items * Hi;
+  const size_t smem = row_smem<S>();
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_fwd_t<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  rows_fwd_t<S><<<(total + SP::ROWS - 1) / SP::ROWS, SP::NWR * 32, smem, st>>>(in, items, Hi, Wi, A, tw, twP);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
 
 template <int S>
-int run_columns(const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP, const int* digrev,
-                const SumJobs& jobs, int njobs, cudaStream_t st) {
-  const int cols = static_lines<S>((size_t)S * sizeof(float2) + 16, 100 * 1024);  // + Ho x cols accumulator (Ho <= S)
-  const size_t smem = (size_t)cols * 2 * (S + 1) * sizeof(float2) + (size_t)cols * S * sizeof(float2);
-  CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  dim3 grid((2 * S + cols - 1) / cols, njobs);
-  columns_s<S><<<grid, kThreads, smem, st>>>(A, Hi, B, Ho, tw, twP, digrev, cols, jobs);
-  CVHRF_LAUNCH_CHECK();
-  return CVHRF_OK;
-}
-
-template <int S>
-int run_rows_inverse(const float2* B, int total_rows, float2* out, int Wo, const float2* tw, const float2* twP,
+int run_rows_inverse(const float2* B, int items, int Ho, float2* out, int Wo, const float2* tw, const float2* twP,
                      int accumulate, cudaStream_t st) {
-  const int rows = static_lines<S>(0);
-  const size_t smem = (size_t)rows * 2 * S * sizeof(float2);
-  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_inverse_s<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  using SP = Split<S>;
+  const int total = items * Ho;
+  const size_t smem = row_smem<S>();
+  CVHRF_CUDA_TRY(cudaFuncSetAttribute(rows_inv_t<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const float P = 2.0f * S;
-  rows_inverse_s<S><<<(total_rows + rows - 1) / rows, kThreads, smem, st>>>(B, total_rows, out, Wo, tw, twP, rows,
-                                                                            1.0f / (P * P), accumulate);
+  rows_inv_t<S><<<(total + SP::ROWS - 1) / SP::ROWS, SP::NWR * 32, smem, st>>>(B, items, Ho, out, Wo, tw, twP,
+                                                                              1.0f / (P * P), accumulate);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
+}
+
+template <int S>
+int run_columns(bool scatter, const float2* A, int Hi, float2* B, int Ho, const ColPlan& plan, const float2* table,
+                const float2* tw, const float2* twP, const int* digrev, cudaStream_t st) {
+  using SP = Split<S>;
+  const size_t smem = col_smem<S>(Hi);
+  if (smem > 227 * 1024) return CVHRF_EUNSUPPORTED;
+  dim3 grid((2 * S + SP::COLS - 1) / SP::COLS, plan.njobs);
+  auto launch = [&](auto kern) -> int {
+    CVHRF_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, SP::NWC * 32, smem, st>>>(A, Hi, B, Ho, plan, table, tw, twP, digrev);
+    CVHRF_LAUNCH_CHECK();
+    return CVHRF_OK;
+  };
+  if (scatter) return table ? launch(cols_scatter_t<S, true>) : launch(cols_scatter_t<S, false>);
+  return table ? launch(cols_sum_t<S, true>) : launch(cols_sum_t<S, false>);
 }
 
 template <int S>
 int run_transfer_table(float2* table, const int* digrev, const TransferTable& tt, int items, cudaStream_t st) {
   const size_t n = (size_t)4 * S * S;
-  const size_t nb = (n + kThreads - 1) / kThreads;
+  const size_t nb = (n + 255) / 256;
   dim3 grid((unsigned)(nb < 1184 ? nb : 1184), items);
-  transfer_table_s<S><<<grid, kThreads, 0, st>>>(table, digrev, tt);
+  transfer_table_s<S><<<grid, 256, 0, st>>>(table, digrev, tt);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
@@ -360,41 +471,9 @@ int run_transfer_table(float2* table, const int* digrev, const TransferTable& tt
 template <int S>
 int run_transfer_upload(float2* table, const int* digrev, const float2* Hc, int items, cudaStream_t st) {
   const size_t n = (size_t)4 * S * S;
-  const size_t nb = (n + kThreads - 1) / kThreads;
+  const size_t nb = (n + 255) / 256;
   dim3 grid((unsigned)(nb < 1184 ? nb : 1184), items);
-  transfer_upload_s<S><<<grid, kThreads, 0, st>>>(table, digrev, Hc);
-  CVHRF_LAUNCH_CHECK();
-  return CVHRF_OK;
-}
-
-// Columns per CTA and threads of the table column passes at S = 1024 (build-time choice).
-#ifndef CVHRF_TABLE_COLS_1024
-#define CVHRF_TABLE_COLS_1024 1
-#endif
-#ifndef CVHRF_TABLE_NT_1024
-#define CVHRF_TABLE_NT_1024 128
-#endif
-
-template <int S>
-int run_columns_table(bool adjoint, const float2* A, int Hi, float2* B, int Ho, const float2* tw, const float2* twP,
-                      const float2* table, int K, int C, cudaStream_t st) {
-  // columns per CTA and threads, measured on B200: 3 columns (96 KB, two CTAs per SM) below
-  // 1024; one column above, with 128 threads where the radix-32 stages have 64 or 128
-  // butterflies per line pair (1024, 2048) and 256 for 1920 (its radix-2 stage is wide)
-  constexpr int COLS = S == 1024 ? CVHRF_TABLE_COLS_1024 : (S > 1024 ? 1 : 3);
-  constexpr int NT = S == 1024 ? CVHRF_TABLE_NT_1024 : (S == 2048 ? 128 : 256);
-  dim3 grid((2 * S + COLS - 1) / COLS, C);
-  if (!adjoint) {
-    const size_t smem = (size_t)COLS * 5 * (S + 1) * sizeof(float2);
-    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_sum_table_s<S, COLS, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)smem));
-    columns_sum_table_s<S, COLS, NT><<<grid, NT, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C);
-  } else {
-    const size_t smem = (size_t)COLS * 4 * (S + 1) * sizeof(float2);
-    CVHRF_CUDA_TRY(cudaFuncSetAttribute(columns_scatter_table_s<S, COLS, NT>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    columns_scatter_table_s<S, COLS, NT><<<grid, NT, smem, st>>>(A, Hi, B, Ho, tw, twP, table, K, C);
-  }
+  transfer_upload_s<S><<<grid, 256, 0, st>>>(table, digrev, Hc);
   CVHRF_LAUNCH_CHECK();
   return CVHRF_OK;
 }
@@ -413,92 +492,62 @@ void static_fft_radices(int S, int* radix, int* nst) {
   case SS: radix[0] = StaticPlan<SS>::r0; radix[1] = StaticPlan<SS>::r1; radix[2] = StaticPlan<SS>::r2; \
     *nst = StaticPlan<SS>::nst; break;
   switch (S) {
-    CVHRF_PLAN(64) CVHRF_PLAN(128) CVHRF_PLAN(256) CVHRF_PLAN(384) CVHRF_PLAN(512) CVHRF_PLAN(800)
-    CVHRF_PLAN(1024) CVHRF_PLAN(1920) CVHRF_PLAN(2048)
+    CVHRF_PLAN(64) CVHRF_PLAN(128) CVHRF_PLAN(256) CVHRF_PLAN(384) CVHRF_PLAN(512)
+    CVHRF_PLAN(1920) CVHRF_PLAN(2048)
+    // the four-step passes keep natural bin order: one "stage" of radix S (identity table)
+    case 800: case 1024: radix[0] = S; *nst = 1; break;
     default: *nst = 0;
   }
 #undef CVHRF_PLAN
 }
 
-int static_rows_forward(const FftDesc& d, const float2* in, int total_rows, int Wi, float2* A, cudaStream_t st) {
-#define CALL run_rows_forward
-#define ARGS (in, total_rows, Wi, A, d.tw, d.twP, st)
-  switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
+// FS: the four-step pass for 800 and 1024 (same arguments), CALL: the warp-line pass.
+#define CVHRF_STATIC_DISPATCH2(CALL, FS, ARGS)                                                             \
+  switch (d.S) {                                                                                           \
+    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;      \
+    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return FS<800> ARGS;      \
+    case 1024: return FS<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS; \
+    default: return CVHRF_EUNSUPPORTED;                                                                    \
   }
-#undef CALL
-#undef ARGS
+#define CVHRF_STATIC_DISPATCH(CALL, ARGS) CVHRF_STATIC_DISPATCH2(CALL, CALL, ARGS)
+
+int static_rows_forward(const FftDesc& d, const float2* in, int items, int Hi, int Wi, float2* A, cudaStream_t st) {
+  CVHRF_STATIC_DISPATCH2(run_rows_forward, fs_run_rows_forward, (in, items, Hi, Wi, A, d.tw, d.twP, st))
 }
 
-int static_columns(const FftDesc& d, const float2* A, int Hi, float2* B, int Ho, const SumJobs& jobs, int njobs,
-                   cudaStream_t st) {
-#define CALL run_columns
-#define ARGS (A, Hi, B, Ho, d.tw, d.twP, d.digrev, jobs, njobs, st)
+int static_columns(const FftDesc& d, bool scatter, const float2* A, int Hi, float2* B, int Ho, const ColPlan& plan,
+                   const float2* table, cudaStream_t st) {
+  if (plan.njobs < 1 || plan.njobs > kMaxColJobs) return CVHRF_EINVAL;
   switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
+    case 800: return fs_run_columns<800>(scatter, A, Hi, B, Ho, plan, table, d.tw, d.twP, st);
+    case 1024: return fs_run_columns<1024>(scatter, A, Hi, B, Ho, plan, table, d.tw, d.twP, st);
+    default: break;
   }
-#undef CALL
-#undef ARGS
+  CVHRF_STATIC_DISPATCH(run_columns, (scatter, A, Hi, B, Ho, plan, table, d.tw, d.twP, d.digrev, st))
 }
 
-int static_rows_inverse(const FftDesc& d, const float2* B, int total_rows, float2* out, int Wo, int accumulate,
+int static_rows_inverse(const FftDesc& d, const float2* B, int items, int Ho, float2* out, int Wo, int accumulate,
                         cudaStream_t st) {
-#define CALL run_rows_inverse
-#define ARGS (B, total_rows, out, Wo, d.tw, d.twP, accumulate, st)
-  switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
-  }
-#undef CALL
-#undef ARGS
+  CVHRF_STATIC_DISPATCH2(run_rows_inverse, fs_run_rows_inverse, (B, items, Ho, out, Wo, d.tw, d.twP, accumulate, st))
 }
 
 int static_transfer_table(const FftDesc& d, float2* table, const TransferTable& tt, int items, cudaStream_t st) {
-#define CALL run_transfer_table
-#define ARGS (table, d.digrev, tt, items, st)
-  switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
-  }
-#undef CALL
-#undef ARGS
+  CVHRF_STATIC_DISPATCH(run_transfer_table, (table, d.digrev, tt, items, st))
 }
 
 int static_transfer_upload(const FftDesc& d, float2* table, const float2* centred, int items, cudaStream_t st) {
-#define CALL run_transfer_upload
-#define ARGS (table, d.digrev, centred, items, st)
-  switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
-  }
-#undef CALL
-#undef ARGS
+  CVHRF_STATIC_DISPATCH(run_transfer_upload, (table, d.digrev, centred, items, st))
 }
 
-int static_columns_table(const FftDesc& d, bool adjoint, const float2* A, int Hi, float2* B, int Ho,
-                         const float2* table, int K, int C, cudaStream_t st) {
-#define CALL run_columns_table
-#define ARGS (adjoint, A, Hi, B, Ho, d.tw, d.twP, table, K, C, st)
-  switch (d.S) {
-    case 64: return CALL<64> ARGS; case 128: return CALL<128> ARGS; case 256: return CALL<256> ARGS;
-    case 384: return CALL<384> ARGS; case 512: return CALL<512> ARGS; case 800: return CALL<800> ARGS;
-    case 1024: return CALL<1024> ARGS; case 1920: return CALL<1920> ARGS; case 2048: return CALL<2048> ARGS;
-    default: return CVHRF_EUNSUPPORTED;
-  }
-#undef CALL
-#undef ARGS
+#undef CVHRF_STATIC_DISPATCH
+#undef CVHRF_STATIC_DISPATCH2
+
+int static_copy_wait_timeouts() {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_copy_wait_timeouts, sizeof(int));
+  return v;
 }
 
 }  // namespace cvhrf
+
+extern "C" int cvhrf_copy_wait_timeouts(void) { return cvhrf::static_copy_wait_timeouts(); }

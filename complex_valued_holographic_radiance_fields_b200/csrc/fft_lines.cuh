@@ -28,51 +28,51 @@ struct FftDesc {
   const int* digrev;           // S entries: position -> natural bin index
 };
 
-// Forward R-point DFTs (sign -1), in registers.
+// Forward R-point DFTs (sign -1), in registers, on the packed f32x2 datapath.
 __device__ __forceinline__ void dft2(float2* x) {
   float2 a = x[0], b = x[1];
-  x[0] = cadd(a, b);
-  x[1] = csub(a, b);
+  x[0] = padd(a, b);
+  x[1] = psub(a, b);
 }
 // multiply by -i
 __device__ __forceinline__ float2 mul_mi(float2 a) { return make_float2(a.y, -a.x); }
 
 __device__ __forceinline__ void dft3(float2* x) {
   const float c = -0.5f, s = 0.86602540378443864676f;
-  float2 t = cadd(x[1], x[2]);
-  float2 d = csub(x[1], x[2]);
-  float2 y0 = cadd(x[0], t);
-  float2 m = make_float2(x[0].x + c * t.x, x[0].y + c * t.y);
-  float2 r = make_float2(s * d.x, s * d.y);       // s (x1 - x2)
+  float2 t = padd(x[1], x[2]);
+  float2 d = psub(x[1], x[2]);
+  float2 y0 = padd(x[0], t);
+  float2 m = pfma(c, t, x[0]);
+  float2 r = pscale(s, d);                         // s (x1 - x2)
   x[0] = y0;
-  x[1] = cadd(m, mul_mi(r));                       // m - i s (x1 - x2)
-  x[2] = csub(m, mul_mi(r));
+  x[1] = padd(m, mul_mi(r));                       // m - i s (x1 - x2)
+  x[2] = psub(m, mul_mi(r));
 }
 
 __device__ __forceinline__ void dft4(float2* x) {
-  float2 a = cadd(x[0], x[2]), b = csub(x[0], x[2]);
-  float2 c = cadd(x[1], x[3]), d = mul_mi(csub(x[1], x[3]));
-  x[0] = cadd(a, c);
-  x[2] = csub(a, c);
-  x[1] = cadd(b, d);
-  x[3] = csub(b, d);
+  float2 a = padd(x[0], x[2]), b = psub(x[0], x[2]);
+  float2 c = padd(x[1], x[3]), d = mul_mi(psub(x[1], x[3]));
+  x[0] = padd(a, c);
+  x[2] = psub(a, c);
+  x[1] = padd(b, d);
+  x[3] = psub(b, d);
 }
 
 __device__ __forceinline__ void dft5(float2* x) {
   const float c1 = 0.30901699437494742410f, c2 = -0.80901699437494742410f;
   const float s1 = 0.95105651629515357212f, s2 = 0.58778525229247312917f;
-  float2 a1 = cadd(x[1], x[4]), b1 = csub(x[1], x[4]);
-  float2 a2 = cadd(x[2], x[3]), b2 = csub(x[2], x[3]);
+  float2 a1 = padd(x[1], x[4]), b1 = psub(x[1], x[4]);
+  float2 a2 = padd(x[2], x[3]), b2 = psub(x[2], x[3]);
   float2 x0 = x[0];
-  float2 r1 = make_float2(x0.x + c1 * a1.x + c2 * a2.x, x0.y + c1 * a1.y + c2 * a2.y);
-  float2 r2 = make_float2(x0.x + c2 * a1.x + c1 * a2.x, x0.y + c2 * a1.y + c1 * a2.y);
-  float2 i1 = make_float2(s1 * b1.x + s2 * b2.x, s1 * b1.y + s2 * b2.y);
-  float2 i2 = make_float2(s2 * b1.x - s1 * b2.x, s2 * b1.y - s1 * b2.y);
-  x[0] = make_float2(x0.x + a1.x + a2.x, x0.y + a1.y + a2.y);
-  x[1] = cadd(r1, mul_mi(i1));
-  x[4] = csub(r1, mul_mi(i1));
-  x[2] = cadd(r2, mul_mi(i2));
-  x[3] = csub(r2, mul_mi(i2));
+  float2 r1 = pfma(c2, a2, pfma(c1, a1, x0));
+  float2 r2 = pfma(c1, a2, pfma(c2, a1, x0));
+  float2 i1 = pfma(s2, b2, pscale(s1, b1));
+  float2 i2 = pfma(-s1, b2, pscale(s2, b1));
+  x[0] = padd(padd(x0, a1), a2);
+  x[1] = padd(r1, mul_mi(i1));
+  x[4] = psub(r1, mul_mi(i1));
+  x[2] = padd(r2, mul_mi(i2));
+  x[3] = psub(r2, mul_mi(i2));
 }
 
 __device__ __forceinline__ void dft8(float2* x) {
@@ -82,13 +82,13 @@ __device__ __forceinline__ void dft8(float2* x) {
   dft4(e);
   dft4(o);
   // o_k *= w8^k
-  o[1] = make_float2(h * (o[1].x + o[1].y), h * (o[1].y - o[1].x));
+  o[1] = pscale(h, make_float2(o[1].x + o[1].y, o[1].y - o[1].x));
   o[2] = mul_mi(o[2]);
-  o[3] = make_float2(h * (o[3].y - o[3].x), -h * (o[3].x + o[3].y));
+  o[3] = pscale(-h, make_float2(o[3].x - o[3].y, o[3].x + o[3].y));
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    x[k] = cadd(e[k], o[k]);
-    x[k + 4] = csub(e[k], o[k]);
+    x[k] = padd(e[k], o[k]);
+    x[k + 4] = psub(e[k], o[k]);
   }
 }
 
@@ -120,14 +120,14 @@ __device__ __forceinline__ void fft_stage(float2* sm, int nlines, int ld, const 
     if constexpr (!INV) {
       dftR<R>(x);
 #pragma unroll
-      for (int m = 1; m < R; ++m) x[m] = cmul(x[m], __ldg(&d.tw[j * m * span]));
+      for (int m = 1; m < R; ++m) x[m] = pmul(x[m], __ldg(&d.tw[j * m * span]));
 #pragma unroll
       for (int m = 0; m < R; ++m) p[m * L] = x[m];
     } else {
 #pragma unroll
       for (int m = 0; m < R; ++m) x[m] = cconj(x[m]);
 #pragma unroll
-      for (int m = 1; m < R; ++m) x[m] = cmul(x[m], __ldg(&d.tw[j * m * span]));
+      for (int m = 1; m < R; ++m) x[m] = pmul(x[m], __ldg(&d.tw[j * m * span]));
       dftR<R>(x);
 #pragma unroll
       for (int m = 0; m < R; ++m) p[m * L] = cconj(x[m]);

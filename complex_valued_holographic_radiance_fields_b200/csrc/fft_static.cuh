@@ -83,7 +83,7 @@ __device__ __forceinline__ float2 twiddle_mul(float2 v) {
   constexpr float c = (float)ct_cos_frac((long)I2 * K1, R);
   constexpr float s = (float)(-ct_sin_frac((long)I2 * K1, R));
   if constexpr (I2 * K1 == 0) return v;
-  else return make_float2(v.x * c - v.y * s, v.x * s + v.y * c);
+  else return pfma(s, make_float2(-v.y, v.x), pscale(c, v));
 }
 
 template <int R, int A, int B, int I2, int K1>
@@ -178,7 +178,7 @@ __device__ __forceinline__ void static_stage(float2* sm, int nlines, int ld, con
       regdft<R>(x);
       if constexpr (L > 1) {
 #pragma unroll
-        for (int m = 1; m < R; ++m) x[m] = cmul(x[m], __ldg(&tw[j * m * span]));
+        for (int m = 1; m < R; ++m) x[m] = pmul(x[m], __ldg(&tw[j * m * span]));
       }
 #pragma unroll
       for (int m = 0; m < R; ++m) p[m * L] = x[m];
@@ -187,7 +187,7 @@ __device__ __forceinline__ void static_stage(float2* sm, int nlines, int ld, con
       for (int m = 0; m < R; ++m) x[m] = cconj(x[m]);
       if constexpr (L > 1) {
 #pragma unroll
-        for (int m = 1; m < R; ++m) x[m] = cmul(x[m], __ldg(&tw[j * m * span]));
+        for (int m = 1; m < R; ++m) x[m] = pmul(x[m], __ldg(&tw[j * m * span]));
       }
       regdft<R>(x);
 #pragma unroll
@@ -250,8 +250,8 @@ __device__ __forceinline__ void static_last_forward_mul_acc(float2* sm, float2* 
     regdft<R>(x);
 #pragma unroll
     for (int m = 0; m < R; ++m) {
-      const float2 y = cmul(x[m], __ldg(&hp[m]));
-      spec[off + m] = first ? y : cadd(spec[off + m], y);
+      const float2 y = pmul(x[m], __ldg(&hp[m]));
+      spec[off + m] = first ? y : padd(spec[off + m], y);
     }
   }
 }
@@ -275,7 +275,7 @@ __device__ __forceinline__ void static_first_inverse_mul(const float2* spec, flo
     const float2* hp = H + ((size_t)(q0 + (line >> 1)) * 2 + (line & 1)) * S + blk * R;
     float2 x[R];
 #pragma unroll
-    for (int m = 0; m < R; ++m) x[m] = cconj(cmul(spec[off + m], cconj(__ldg(&hp[m]))));
+    for (int m = 0; m < R; ++m) x[m] = cconj(pmul(spec[off + m], cconj(__ldg(&hp[m]))));
     regdft<R>(x);
 #pragma unroll
     for (int m = 0; m < R; ++m) sm[off + m] = cconj(x[m]);

@@ -1,4 +1,4 @@
-// The caller's glue around the rasterizer, fused (SURVEY next-step f1; replaces the torch
+// The caller's glue around the rasterizer, fused (replaces the torch
 // ops of model.py:1365-1402 Scene.render and model.py:595-608 apply_activations):
 //
 //   forward : X_cam = X @ R + T; keep near < z < far; sort by depth; gather every

@@ -398,6 +398,12 @@ size_t cvhrf_inclusive_scan_workspace_bytes(int n);
 int cvhrf_inclusive_scan_u32(const uint32_t* in, uint32_t* out, int n, void* workspace,
                              size_t workspace_bytes, void* stream);
 int cvhrf_lookback_timeouts(void);
+/*
+ * How many waits of the propagation column passes on their bulk (TMA) column copies ran
+ * out of their iteration limit since the library was loaded (each invalidates that call's
+ * result; expected 0; synchronises).
+ */
+int cvhrf_copy_wait_timeouts(void);
 
 /* ---- L2 intensity loss of the training iteration --------------------------- */
 /*

@@ -161,3 +161,13 @@ def test_planes_vs_oracle(cuda, S, H, W, K, C, use_table):
         for c in range(C):
             exp_g = O.propagate(g_np[c], wl[c], 8e-6, -ds[p], S, float(S), out_hw=(H, W))
             assert rel(fr.grad[p, c], exp_g) < TOL, (p, c)
+
+
+def test_no_copy_wait_timeouts(cuda):
+    """The column passes' bulk-copy waits never ran out of their limit in this process."""
+    from complex_valued_holographic_radiance_fields_b200 import _lib
+    from complex_valued_holographic_radiance_fields_b200 import propagation as P
+    x = rand_field(800, 800, 3).to(cuda)
+    P.propagate(x, 532e-9, 8e-6, 1e-3, 800, 800.0)
+    torch.cuda.synchronize()
+    assert _lib.lib().cvhrf_copy_wait_timeouts() == 0
