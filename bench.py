@@ -109,8 +109,18 @@ def fp32_peak_tflops(sm_mhz):
 
 
 # arithmetic of the reference's per-(pixel, Gaussian) backward body (backward_splat.cu:184-300)
-# for C = 3, counted once: power 6, alpha 3, T 2, 3 channels x 21, alpha/geometry/conic/cov 36
+# for C = 3, counted once: power 6, alpha 3, T 2, 3 channels x 21, alpha/geometry/conic/cov 36.
+# Only a contributing evaluation (power <= 0 and alpha >= 1/255) runs that body; any other
+# evaluation of a (pixel, Gaussian) pair of the tile lists stops after the offset, the
+# quadratic form and the alpha test (about 10 FLOP).  The share of contributing evaluations
+# among the 256 x pairs was counted once with the CVHRF_BWD_STATS build of
+# render_backward_kernel at this workload (87,050,739 of 632,232,960;
+# profiles/ncu_render_backward_config3.md).
 BWD_FLOP_PER_EVAL = 110
+BWD_FLOP_PER_SKIPPED_EVAL = 10
+BWD_CONTRIB_FRACTION = 87050739 / 632232960
+# FMA-pipe utilisation of render_backward_kernel<3> measured by ncu at this workload (same file)
+BWD_FMA_PIPE_PCT = 34.4
 # dram__bytes_read.sum + dram__bytes_write.sum of render_backward_kernel<3> at this workload
 # (profiles/ncu_hot_kernels_config3_train_step.md)
 BWD_NCU_TRAFFIC = 297.1e6
@@ -241,14 +251,19 @@ def run_mine(args, world, rank, local):
     # dominant operator: the rasterizer backward, bound by the FP32 pipe (not HBM, not tensor cores)
     from complex_valued_holographic_radiance_fields_b200 import rasterizer as RZ
     evals = 256.0 * RZ.last_num_pairs          # pixel x (tile, Gaussian) pair evaluations, one plane each
+    contrib = evals * BWD_CONTRIB_FRACTION
+    bwd_flop = contrib * BWD_FLOP_PER_EVAL + (evals - contrib) * BWD_FLOP_PER_SKIPPED_EVAL
     bwd_ms = opsum.get("raster_backward", (1, float("nan")))[1]
     sm_mhz = clocks.get("sm_mhz") or 1965.0
     peak_tf = fp32_peak_tflops(sm_mhz)
     roof = {"op": "raster_backward (render_backward_kernel + gaussian_grad_kernel)", "bound": "fp32",
-            "achieved": evals * BWD_FLOP_PER_EVAL / (bwd_ms * 1e-3) / 1e12, "peak": peak_tf, "unit": "TFLOP/s",
+            "achieved": bwd_flop / (bwd_ms * 1e-3) / 1e12, "peak": peak_tf, "unit": "TFLOP/s",
             "peak_source": f"SMs x 128 FMA lanes x 2 x median SM clock {sm_mhz:.0f} MHz (no tensor-core work)",
-            "algorithmic_flop": evals * BWD_FLOP_PER_EVAL,
-            "work_unit": f"{BWD_FLOP_PER_EVAL} FLOP per pixel-pair evaluation x 256 x {RZ.last_num_pairs} pairs",
+            "algorithmic_flop": bwd_flop,
+            "work_unit": (f"{BWD_FLOP_PER_EVAL} FLOP per contributing pixel-Gaussian evaluation "
+                          f"({BWD_CONTRIB_FRACTION:.4f} of 256 x {RZ.last_num_pairs} pairs), "
+                          f"{BWD_FLOP_PER_SKIPPED_EVAL} per other evaluation"),
+            "fma_pipe_pct_ncu": BWD_FMA_PIPE_PCT,
             "traffic": BWD_NCU_TRAFFIC}
     roof["frac"] = roof["achieved"] / peak_tf
     line = {

@@ -26,48 +26,55 @@ __device__ unsigned long long g_bwd_stats[8];
 
 namespace {
 
-constexpr int kRedV = 16;  // padded length of the per-Gaussian vector that is reduced
+constexpr int kRedV = 12;  // length of the per-Gaussian vector that is reduced
 
 // floats per (tile, Gaussian) record: 6 + K + 2C rounded up to a multiple of 4
 __host__ __device__ __forceinline__ int record_stride(int K, int C) { return (6 + K + 2 * C + 3) & ~3; }
 
-// Sum v[0..15] over the warp; afterwards every even lane l holds the total of index (l >> 1).
-__device__ __forceinline__ float warp_reduce_scatter16(float (&v)[kRedV]) {
+// Sum v[0..11] over the warp (reduce-scatter: each exchange hands half of a lane's live
+// sums to its partner).  Afterwards the total of index 3i + j (i < 4, j < 3) is held by
+// lane 8i + {0, 4, 2}[j] (reduce12_slot gives the index a lane holds, or -1).  13 shuffles
+// for 12 sums.
+__device__ __forceinline__ float warp_reduce_scatter12(float (&v)[kRedV]) {
   const int lane = threadIdx.x & 31;
-  {
+  {  // 12 -> 6
     const bool hi = lane & 16;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float send = hi ? v[i] : v[i + 8];
-      const float keep = hi ? v[i + 8] : v[i];
+    for (int i = 0; i < 6; ++i) {
+      const float send = hi ? v[i] : v[i + 6];
+      const float keep = hi ? v[i + 6] : v[i];
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
   }
-  {
+  {  // 6 -> 3
     const bool hi = lane & 8;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float send = hi ? v[i] : v[i + 4];
-      const float keep = hi ? v[i + 4] : v[i];
+    for (int i = 0; i < 3; ++i) {
+      const float send = hi ? v[i] : v[i + 3];
+      const float keep = hi ? v[i + 3] : v[i];
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
   }
-  {
+  // lane (bits 4, 3 = b) now holds sums 6 b4 + 3 b3 + (0..2) over its 8-lane group
+  {  // 3 -> 2 (the third sum rides along)
     const bool hi = lane & 4;
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const float send = hi ? v[i] : v[i + 2];
-      const float keep = hi ? v[i + 2] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-  }
-  {
-    const bool hi = lane & 2;
     const float send = hi ? v[0] : v[1];
     const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    v[2] += __shfl_xor_sync(0xffffffffu, v[2], 4);
+  }
+  {  // 2 -> 1
+    const bool hi = lane & 2;
+    const float send = hi ? v[0] : v[2];
+    const float keep = hi ? v[2] : v[0];
     v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
   }
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+__device__ __forceinline__ int reduce12_slot(int lane) {
+  if ((lane & 1) || (lane & 6) == 6) return -1;
+  const int j = (lane & 2) ? 2 : ((lane & 4) ? 1 : 0);
+  return 3 * (lane >> 3) + j;
 }
 
 // Per-Gaussian constants of the backward pixel loop, computed once per batch with the
@@ -130,7 +137,8 @@ __device__ __forceinline__ void bwd_pair(PairState<C>& st, const float4 con, flo
                                          float2 power, bool n0, bool n1, const float2* cpx, float* r) {
   // con = (conic_x, conic_y, conic_z, opacity); power = pair_power(con, dx, dy)
   const float2 dy2 = make_float2(dy, dy);
-  const float2 G = make_float2(expf(power.x), expf(power.y));
+  // __expf: the gradients are compared at 1e-4, and ex2.approx is within a few ulp
+  const float2 G = make_float2(__expf(power.x), __expf(power.y));
   const float2 aw = __fmul2_rn(__fmul2_rn(make_float2(con.w, con.w), G), make_float2(w, w));
   const float al0 = fminf(0.99f, aw.x), al1 = fminf(0.99f, aw.y);
   const bool a0 = n0 && power.x <= 0.0f && al0 >= 1.0f / 255.0f;
@@ -186,7 +194,7 @@ __global__ void __launch_bounds__(128, 6) render_backward_kernel(
     const int32_t* __restrict__ n_contrib, const float2* __restrict__ grad_field, int K, int W, int H, int gx,
     float* __restrict__ records, const int32_t* __restrict__ tile_order) {
   constexpr int NB = 128, NW = 4, RL = red_len<C>(), RP = RL;
-  static_assert(RL <= kRedV, "reduction vector too long");
+  static_assert(RL <= 12, "reduction vector too long");
   __shared__ uint32_t s_slot[NB];
   __shared__ float4 s_geo[NB];      // (mean x, mean y, box half-width, box half-height): the footprint test
   __shared__ float4 s_wq[NB];       // (plane weight, list position, -ln(255 opacity weight), Gaussian) (ints as bits)
@@ -215,6 +223,7 @@ __global__ void __launch_bounds__(128, 6) render_backward_kernel(
   const float tx0 = (float)(tx * kTile), tx1 = (float)(tx * kTile + kTile - 1);
   const float ty0 = (float)(ty * kTile), ty1 = (float)(ty * kTile + kTile - 1);
   const unsigned lt = (1u << lane) - 1u;
+  const int slot12 = reduce12_slot(lane);
 
   for (int p = 0; p < K; ++p) {
     PairState<C> st;
@@ -339,9 +348,9 @@ __global__ void __launch_bounds__(128, 6) render_backward_kernel(
         for (int c = 0; c < C; ++c) cpx[c] = s_cpx[c][jj];
         bwd_pair<C>(st, con, wq.x, dx, dy, power, c0, c1, cpx, v);
 #pragma unroll
-        for (int i = RL; i < kRedV; ++i) v[i] = 0.f;
-        const float tot = warp_reduce_scatter16(v);
-        if ((lane & 1) == 0 && (lane >> 1) < RL) s_part[warp][jj][lane >> 1] = tot;
+        for (int i = RL; i < 12; ++i) v[i] = 0.f;
+        const float tot = warp_reduce_scatter12(v);
+        if (slot12 >= 0 && slot12 < RL) s_part[warp][jj][slot12] = tot;
       }
       __syncthreads();
       // ---- the pair's record share: the warps' sums, per-Gaussian factors applied once ----
@@ -382,8 +391,9 @@ __global__ void __launch_bounds__(128, 6) render_backward_kernel(
           }
         }
         const int ri = idx < 6 ? idx : (idx == 6 ? 6 + p : 6 + K + (idx - 7));
-        float* dst = records + (size_t)s_slot[j] * VR + ri;
-          *dst += val;
+        // a reduction without return (red.global.add): the record's earlier planes were
+        // added batches ago by this block, so the order of additions is the plane order
+        atomicAdd(records + (size_t)s_slot[j] * VR + ri, val);
       }
     }
   }
