@@ -725,6 +725,30 @@ def _ref_cuda_component(args):
             "what": "reference cov3d_cuda Rasterizer.forward (rebuilt sm_100a)"}
 
 
+def strong_records(args, world, rank, local):
+    """The two strong-scaling workloads, measured in the same process after the headline
+    (which is config-3 weak scaling): config 4 (the 8 views of one iteration split over
+    the GPUs) and config 5 (the 7 planes of one iteration split over the GPUs).  Each is
+    timed like its own --workload line (warm-up, then device-timed steps, max over ranks)."""
+    import gc
+    out = {}
+    for key, fn, steps, warmup in (("strong_config4", run_config4, min(args.steps, 5), 2),
+                                   ("strong_config5", run_config5, min(args.steps, 10), 3)):
+        gc.collect()
+        torch.cuda.empty_cache()
+        sub = argparse.Namespace(**vars(args))
+        sub.steps, sub.warmup = steps, warmup
+        try:
+            r = fn(sub, world, rank, local)
+        except Exception as e:  # a failed sub-record must not lose the headline line
+            r = {"unavailable": repr(e)[:300]}
+        if r is not None:
+            keep = ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "config",
+                    "execution", "unavailable")
+            out[key] = {k: v for k, v in r.items() if k in keep}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -732,6 +756,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="skip the strong-scaling sub-records (config 4 and 5) of the default line")
     ap.add_argument("--workload", default="config3", choices=["config1", "config2", "config3", "config3mp", "config4",
                                                            "config5"],
                     help="config1 / config2 (the propagation / rasterizer forward alone), "
@@ -761,6 +787,10 @@ def main():
             line = run_mine(args, world, rank, local)
             if line is not None and world == 1 and not args.no_cpu_baseline and args.workload == "config3":
                 line["cpu_baseline"] = cpu_baseline(samples=3, warmup=1)
+            if args.workload == "config3" and not args.no_strong:
+                strong = strong_records(args, world, rank, local)
+                if line is not None:
+                    line.update(strong)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

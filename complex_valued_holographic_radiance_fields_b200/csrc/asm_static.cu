@@ -50,12 +50,20 @@ namespace {
 // Work split per line length (the warp-line passes: sizes other than 800 and 1024).
 template <int S>
 struct Split {
-  static constexpr int RPW = S >= 800 ? 1 : (S >= 256 ? 2 : 4);  // rows per warp (row passes)
-  static constexpr int NWR = S >= 1024 ? 4 : 8;                  // warps per block (row passes)
-  static constexpr int ROWS = RPW * NWR;                         // rows per block (row passes)
-  static constexpr int LPW = S >= 800 ? 1 : (S >= 256 ? 2 : 4);  // lines per warp (column passes)
-  static constexpr int COLS = S == 800 ? 3 : (S == 1024 ? 2 : (S > 1024 ? 1 : 4));  // columns per block
-  static constexpr int NWC = 2 * COLS / LPW;                     // warps per block (column passes)
+  // For the longest lines (BLK) a whole block transforms its lines together (one warp per
+  // 1920- or 2048-point line would leave too few warps per SM to hide the shared-memory
+  // latency of its stages); otherwise each warp owns its lines.
+  static constexpr bool BLK = S >= 1920;
+  // row passes: RPW rows per warp, NWR warps, ROWS rows per block, NTR threads per row group
+  static constexpr int RPW = S >= 800 ? 1 : (S >= 256 ? 2 : 4);
+  static constexpr int NWR = BLK ? 8 : (S >= 1024 ? 4 : 8);
+  static constexpr int ROWS = BLK ? 2 : RPW * NWR;
+  static constexpr int NTR = BLK ? NWR * 32 : 32;
+  // column passes: COLS columns per block, LPW lines per group, NWC warps, NTH threads per group
+  static constexpr int COLS = S == 800 ? 3 : (S == 1024 ? 2 : (S > 1024 ? 1 : 4));
+  static constexpr int LPW = BLK ? 2 * COLS : (S >= 800 ? 1 : (S >= 256 ? 2 : 4));
+  static constexpr int NWC = BLK ? 8 : 2 * COLS / LPW;
+  static constexpr int NTH = BLK ? NWC * 32 : 32;
   static constexpr int LD = line_ld(S);
 };
 
@@ -72,36 +80,35 @@ __global__ void __launch_bounds__(Split<S>::NWR * 32) rows_fwd_t(const float2* _
   const int total = items * Hi;
   const int row0 = blockIdx.x * ROWS;
   const int ow = (P - Wi) / 2;
-  // each warp loads and folds its rows: line 2r holds x[n] at n mod S, line 2r + 1 holds
-  // x[n] w_2S^n (the odd output bins).  The loads are asynchronous copies, all in flight
-  // at once; the odd lines are formed once they land.
-  for (int rr = 0; rr < SP::RPW; ++rr) {
-    const int r = warp * SP::RPW + rr;
+  // each row group (a warp, or the whole block) loads and folds its rows: line 2r holds
+  // x[n] at n mod S, line 2r + 1 holds x[n] w_2S^n (the odd output bins).  The loads are
+  // asynchronous copies, all in flight at once; the odd lines are formed once they land.
+  constexpr int GN = SP::NTR;
+  const int gt = SP::BLK ? (int)threadIdx.x : lane;
+  const int gr0 = SP::BLK ? 0 : warp * SP::RPW, grn = SP::BLK ? ROWS : SP::RPW;
+  for (int e = gt; e < grn * S; e += GN) {
+    const int r = gr0 + e / S, t = e % S;
     const int g = row0 + r;
     float2* le = sm + (2 * r) * LD;
     const float2* src = in + (size_t)(g < total ? g : 0) * Wi;
-    for (int t = lane; t < S; t += 32) {
-      int j = t - ow;
-      if (j < 0 || j >= Wi) j = t + S - ow;
-      if (g < total && j >= 0 && j < Wi) cp_async8(le + pidx(t), src + j);
-      else le[pidx(t)] = make_float2(0.f, 0.f);
-    }
+    int j = t - ow;
+    if (j < 0 || j >= Wi) j = t + S - ow;
+    if (g < total && j >= 0 && j < Wi) cp_async8(le + pidx(t), src + j);
+    else le[pidx(t)] = make_float2(0.f, 0.f);
   }
   cp_async_commit();
   cp_async_wait_all();
-  __syncwarp();
-  for (int rr = 0; rr < SP::RPW; ++rr) {
-    const int r = warp * SP::RPW + rr;
+  group_sync<GN>();
+  for (int e = gt; e < grn * S; e += GN) {
+    const int r = gr0 + e / S, t = e % S;
     const float2* le = sm + (2 * r) * LD;
     float2* lo = sm + (2 * r + 1) * LD;
-    for (int t = lane; t < S; t += 32) {
-      const int j = t - ow;
-      const int pos = (j < 0 || j >= Wi) ? t + S : t;
-      lo[pidx(t)] = pmul(le[pidx(t)], __ldg(&twP[pos]));
-    }
+    const int j = t - ow;
+    const int pos = (j < 0 || j >= Wi) ? t + S : t;
+    lo[pidx(t)] = pmul(le[pidx(t)], __ldg(&twP[pos]));
   }
-  __syncwarp();
-  warp_fft_forward<S>(sm + (2 * warp * SP::RPW) * LD, 2 * SP::RPW, lane, tw);
+  group_sync<GN>();
+  warp_fft_forward<S, GN>(sm + (2 * gr0) * LD, 2 * grn, gt, tw);
   __syncthreads();
   // transposed store: for every spectrum column q, the block's ROWS rows are one run
   const int HiS = col_stride(Hi);
@@ -144,30 +151,30 @@ __global__ void __launch_bounds__(Split<S>::NWR * 32) rows_inv_t(const float2* _
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
-  warp_fft_inverse<S>(sm + (2 * warp * SP::RPW) * LD, 2 * SP::RPW, lane, tw);
+  constexpr int GN = SP::NTR;
+  const int gt = SP::BLK ? (int)threadIdx.x : lane;
+  const int gr0 = SP::BLK ? 0 : warp * SP::RPW, grn = SP::BLK ? ROWS : SP::RPW;
+  warp_fft_inverse<S, GN>(sm + (2 * gr0) * LD, 2 * grn, gt, tw);
   const int oc = (P - Wo) / 2;
-  for (int rr = 0; rr < SP::RPW; ++rr) {
-    const int r = warp * SP::RPW + rr;
+  for (int e = gt; e < grn * Wo; e += GN) {
+    const int r = gr0 + e / Wo, x = e % Wo;
     const int g = row0 + r;
-    if (g >= total) break;
+    if (g >= total) continue;
     const float2* le = sm + (2 * r) * LD;
     const float2* lo = le + LD;
-    float2* dst = out + (size_t)g * Wo;
-    for (int x = lane; x < Wo; x += 32) {
-      const int n = oc + x;
-      const int t = n >= S ? n - S : n;
-      float2 v = padd(le[pidx(t)], pmul(cconj(__ldg(&twP[n])), lo[pidx(t)]));
-      v.x *= scale;
-      v.y *= scale;
-      if (accumulate) v = padd(dst[x], v);
-      dst[x] = v;
-    }
+    const int n = oc + x;
+    const int t = n >= S ? n - S : n;
+    float2 v = padd(le[pidx(t)], pmul(cconj(__ldg(&twP[n])), lo[pidx(t)]));
+    v = pscale(scale, v);
+    float2* dst = out + (size_t)g * Wo + x;
+    if (accumulate) v = padd(*dst, v);
+    *dst = v;
   }
 }
 
 // Fill this warp's lines (line gl = 2 cc + h of the block) from the staged columns:
 // the even half-line takes the column, the odd one the column times w_2S^n.
-template <int S>
+template <int S, int NTH = 32>
 __device__ __forceinline__ void fold_columns(float2* lines, int gl0, int nl, const float2* stage, int HiS, int Hi,
                                              int lane, const float2* __restrict__ twP) {
   constexpr int P = 2 * S, LD = line_ld(S);
@@ -177,7 +184,7 @@ __device__ __forceinline__ void fold_columns(float2* lines, int gl0, int nl, con
     const float2* col = stage + cc * HiS;
     float2* line = lines + l * LD;
 #pragma unroll 4
-    for (int t = lane; t < S; t += 32) {
+    for (int t = lane; t < S; t += NTH) {
       int r = t - oh, pos = t;
       if (r < 0 || r >= Hi) { r = t + S - oh; pos = t + S; }
       float2 v = make_float2(0.f, 0.f);
@@ -185,7 +192,7 @@ __device__ __forceinline__ void fold_columns(float2* lines, int gl0, int nl, con
       line[pidx(t)] = h ? pmul(v, __ldg(&twP[pos])) : v;
     }
   }
-  __syncwarp();
+  group_sync<NTH>();
 }
 
 // ---- pass B, sum form: out[job] = sum_k P_k(in[k]) per column ------------------------
@@ -210,7 +217,9 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_sum_t(const float2
   float2* stage = sm;
   float2* work = sm + ((COLS * HiS + 1) & ~1);
   float2* spec = work + 2 * COLS * LD;
-  const int gl0 = warp * LPW;
+  constexpr int NTH = SP::NTH;
+  const int gt = SP::BLK ? (int)threadIdx.x : lane;    // thread index within the line group
+  const int gl0 = SP::BLK ? 0 : warp * LPW;
   const int nl = max(0, min(LPW, 2 * ncols - gl0));
   float2* wl = work + gl0 * LD;
   float2* sl = spec + gl0 * LD;
@@ -238,17 +247,17 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_sum_t(const float2
   }
   for (int k = 0; k < nin; ++k) {
     wait_copies(&bar, k & 1);
-    fold_columns<S>(wl, gl0, nl, stage, HiS, Hi, lane, twP);
+    fold_columns<S, NTH>(wl, gl0, nl, stage, HiS, Hi, gt, twP);
     __syncthreads();                       // every warp is done with the staging buffer
     if (threadIdx.x == 0 && k + 1 < nin) {
       fence_proxy_async_smem();
       issue(k + 1);
     }
-    warp_fft_forward_head<S>(wl, nl, lane, tw);
+    warp_fft_forward_head<S, NTH>(wl, nl, gt, tw);
     const int ti = plan.tpi[job][k];
     if constexpr (TABLE) {
       const float2* Hb = table + (size_t)ti * P * P;
-      warp_last_forward_mul_acc<S>(wl, sl, nl, lane, k == 0, [&](int l, int pos) {
+      warp_last_forward_mul_acc<S, NTH>(wl, sl, nl, gt, k == 0, [&](int l, int pos) {
         const int gl = gl0 + l;
         return __ldg(&Hb[((size_t)(q0 + (gl >> 1)) * 2 + (gl & 1)) * S + pos]);
       });
@@ -257,7 +266,7 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_sum_t(const float2
       TransferCol col[LPW];
 #pragma unroll
       for (int l = 0; l < LPW; ++l) col[l] = transfer_col(kv[l], P, tp);
-      warp_last_forward_mul_acc<S>(wl, sl, nl, lane, k == 0, [&](int l, int pos) {
+      warp_last_forward_mul_acc<S, NTH>(wl, sl, nl, gt, k == 0, [&](int l, int pos) {
         const int ku = 2 * __ldg(&digrev[pos]) + ((gl0 + l) & 1);
         TransferCol c = col[0];
 #pragma unroll
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_sum_t(const float2
       });
     }
   }
-  warp_fft_inverse<S>(sl, nl, lane, tw);
+  warp_fft_inverse<S, NTH>(sl, nl, gt, tw);
   __syncthreads();
   // crop and fold back: y[n] = e[n mod S] + w_2S^-n o[n mod S]; each column is one run
   const int oc = (P - Ho) / 2;
@@ -302,7 +311,9 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_scatter_t(const fl
   float2* stage = sm;
   float2* work = sm + ((COLS * HiS + 1) & ~1);
   float2* spec = work + 2 * COLS * LD;
-  const int gl0 = warp * LPW;
+  constexpr int NTH = SP::NTH;
+  const int gt = SP::BLK ? (int)threadIdx.x : lane;    // thread index within the line group
+  const int gl0 = SP::BLK ? 0 : warp * LPW;
   const int nl = max(0, min(LPW, 2 * ncols - gl0));
   float2* wl = work + gl0 * LD;
   float2* sl = spec + gl0 * LD;
@@ -325,15 +336,15 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_scatter_t(const fl
     kv[l] = 2 * __ldg(&digrev[q - qh * S]) + qh;
   }
   wait_copies(&bar, 0);
-  fold_columns<S>(sl, gl0, nl, stage, HiS, Hi, lane, twP);
-  warp_fft_forward<S>(sl, nl, lane, tw);
+  fold_columns<S, NTH>(sl, gl0, nl, stage, HiS, Hi, gt, twP);
+  warp_fft_forward<S, NTH>(sl, nl, gt, tw);
   const int oc = (P - Ho) / 2;
   const int nout = plan.n[job];
   for (int k = 0; k < nout; ++k) {
     const int ti = plan.tpi[job][k];
     if constexpr (TABLE) {
       const float2* Hb = table + (size_t)ti * P * P;
-      warp_first_inverse_mul<S>(sl, wl, nl, lane, [&](int l, int pos) {
+      warp_first_inverse_mul<S, NTH>(sl, wl, nl, gt, [&](int l, int pos) {
         const int gl = gl0 + l;
         return __ldg(&Hb[((size_t)(q0 + (gl >> 1)) * 2 + (gl & 1)) * S + pos]);
       });
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_scatter_t(const fl
       TransferCol col[LPW];
 #pragma unroll
       for (int l = 0; l < LPW; ++l) col[l] = transfer_col(kv[l], P, tp);
-      warp_first_inverse_mul<S>(sl, wl, nl, lane, [&](int l, int pos) {
+      warp_first_inverse_mul<S, NTH>(sl, wl, nl, gt, [&](int l, int pos) {
         const int ku = 2 * __ldg(&digrev[pos]) + ((gl0 + l) & 1);
         TransferCol c = col[0];
 #pragma unroll
@@ -351,7 +362,7 @@ __global__ void __launch_bounds__(Split<S>::NWC * 32, 2) cols_scatter_t(const fl
         return transfer_row(ku, P, c, tp);
       });
     }
-    warp_fft_inverse_rest<S>(wl, nl, lane, tw);
+    warp_fft_inverse_rest<S, NTH>(wl, nl, gt, tw);
     __syncthreads();
     float2* Bout = B + ((size_t)plan.items[job][k] * P + q0) * HoS;
     for (int e = threadIdx.x; e < ncols * Ho; e += NT) {
