@@ -27,6 +27,10 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
 ARCH = "-gencode=arch=compute_100a,code=sm_100a"
+# --ptx80: the same sources as compute_80 PTX only (JIT-compiled by the driver on a B200),
+# into oracle/_ref80/ -- the "reference's own sm_80 build run on a B200" comparison point
+OUT80 = os.path.join(HERE, "_ref80")
+ARCH80 = "-gencode=arch=compute_80,code=compute_80"
 
 
 def _load(name, sources, include_dirs, cuda_flags, build_dir):
@@ -37,7 +41,7 @@ def _load(name, sources, include_dirs, cuda_flags, build_dir):
                 build_directory=build_dir, verbose=False, is_python_module=True)
 
 
-def build(ref_root="/root/reference"):
+def build(ref_root="/root/reference", arch=ARCH, out=OUT):
     cov = os.path.join(ref_root, "cuda_prop", "cov3d_cuda")
     prop = os.path.join(ref_root, "cuda_prop")
     if not os.path.isdir(cov):
@@ -50,8 +54,8 @@ def build(ref_root="/root/reference"):
                                            "backward_splat.cu", "rasterizer_splat.cu")]
           + [os.path.join(cov, "conv.cu")],
           [os.path.join(cov, "third_party", "glm")],
-          ["-O3", "-DTORCH_USE_CUDA_DSA", "-diag-suppress=20012", ARCH],
-          os.path.join(OUT, "cov3d_cuda_ref"))
+          ["-O3", "-DTORCH_USE_CUDA_DSA", "-diag-suppress=20012", arch],
+          os.path.join(out, "cov3d_cuda_ref"))
     cpp = os.path.join(prop, "cpp")
     cu = os.path.join(prop, "cuda")
     _load("cuda_modules_ref",
@@ -59,7 +63,7 @@ def build(ref_root="/root/reference"):
                                           "sum_last_dim.cpp", "element_wise_mult.cpp", "module_def.cpp")]
           + [os.path.join(cu, f) for f in ("bandlimited_propagation_cuda.cu", "batch_matrix_mult_cuda.cu",
                                            "sum_last_dim_cuda.cu", "element_wise_mult_cuda.cu")],
-          [], ["-O3", ARCH], os.path.join(OUT, "cuda_modules_ref"))
+          [], ["-O3", arch], os.path.join(out, "cuda_modules_ref"))
 
 
 def built():
@@ -70,6 +74,7 @@ def built():
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ptx80", action="store_true")
     a = ap.parse_args()
-    build(a.ref)
-    print("built reference modules under", OUT)
+    build(a.ref, ARCH80, OUT80) if a.ptx80 else build(a.ref)
+    print("built reference modules under", OUT80 if a.ptx80 else OUT)

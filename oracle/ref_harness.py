@@ -18,7 +18,8 @@ import sys
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-REF_DIR = os.path.join(_HERE, "_ref")
+# CVHRF_REF_DIR selects another build of the same modules (oracle/_ref80: compute_80 PTX)
+REF_DIR = os.environ.get("CVHRF_REF_DIR") or os.path.join(_HERE, "_ref")
 
 
 def available():
