@@ -292,7 +292,10 @@ class PlaneShardedTrainer(HoloTrainer):
             return super().forward(target)
         from .distributed import all_reduce_sum
         C = len(self.wavelengths)
-        holo = all_reduce_sum(torch.zeros((C, self.S, self.S), dtype=torch.complex64, device=self.device), self.group)
+        # the zeros take part in autograd so that loss.backward() runs on this rank as on the
+        # others (its Gaussian gradients stay absent and are sent as zeros in the exchange)
+        zeros = torch.zeros((C, self.S, self.S), dtype=torch.complex64, device=self.device, requires_grad=True)
+        holo = all_reduce_sum(zeros, self.group)
         loss = self._loss(holo, self.target if target is None else target)
         return loss, torch.empty(0, dtype=torch.long, device=self.device)
 

@@ -86,3 +86,35 @@ def test_two_gpu_view_and_plane_parallel():
     assert res[0]["loss_err"] < 1e-5, res[0]
     assert res[0]["param_err"] < 1e-3, res[0]   # Adam normalises: near-zero gradients amplify rounding
     assert all(p.exitcode == 0 for p in ps)
+
+
+def _idle_rank_worker(port, q):
+    """One process, NCCL world of 1, a plane-parallel trainer that owns no plane (the case of
+    a GPU beyond the plane count, e.g. K = 7 over 8 GPUs): its step must run the same
+    collectives as an owning rank and leave the parameters unchanged (zero gradients)."""
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev)
+    from complex_valued_holographic_radiance_fields_b200.train_step import PlaneShardedTrainer
+    tr = PlaneShardedTrainer(N=5000, W=96, H=96, K=2, device=dev, rank=0, world=1)
+    tr.planes, tr.owned_mask = [], 0
+    tr.world = 2            # take the multi-rank exchange path (the group itself has one rank)
+    before = {k: v.detach().clone() for k, v in tr.params.items()}
+    loss = float(tr.step())
+    torch.cuda.synchronize()
+    same = all(torch.equal(before[k], v.detach()) for k, v in tr.params.items())
+    dist.destroy_process_group()
+    q.put((loss, same))
+
+
+def test_rank_without_planes_steps(cuda):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_idle_rank_worker, args=(_free_port(), q))
+    p.start()
+    p.join(300)
+    assert p.exitcode == 0
+    loss, same = q.get(timeout=5)
+    assert loss == loss and same
