@@ -120,13 +120,13 @@ BWD_FLOP_PER_EVAL = 110
 BWD_FLOP_PER_SKIPPED_EVAL = 10
 BWD_CONTRIB_FRACTION = 87050739 / 632232960
 # FMA-pipe utilisation of render_backward_kernel<3> measured by ncu at this workload (same file)
-BWD_FMA_PIPE_PCT = 34.4
+BWD_FMA_PIPE_PCT = 36.9
 # dram__bytes_read.sum + dram__bytes_write.sum of render_backward_kernel<3> at this workload
-# (profiles/ncu_hot_kernels_config3_train_step.md)
-BWD_NCU_TRAFFIC = 297.1e6
-# the same for the forward propagation's three kernels (rows_forward_s, columns_sum_table_s,
-# rows_inverse_s; profiles/ncu_propagation_config3.md)
-PROP_NCU_TRAFFIC = 413.6e6
+# (profiles/ncu_render_backward_config3.md)
+BWD_NCU_TRAFFIC = 283.5e6
+# the same for the forward propagation's three kernels (fs_rows_fwd, fs_cols_sum, fs_rows_inv;
+# profiles/ncu_propagation_config3.md)
+PROP_NCU_TRAFFIC = 417.0e6
 
 
 def peaks():
