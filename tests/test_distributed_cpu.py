@@ -81,3 +81,41 @@ def test_plane_ownership():
     owned = [[p for p in range(7) if p % 8 == r] for r in range(8)]
     assert owned[7] == [] and sorted(sum(owned, [])) == list(range(7))
     assert PlaneShardedTrainer.__mro__[1].__name__ == "HoloTrainer"
+
+
+def _worker_idle_rank(rank, world, port, q):
+    """Rank 1 renders nothing (a GPU beyond the plane count): it contributes a zero hologram
+    that takes part in autograd, so its loss.backward() runs like rank 0's and both ranks
+    issue the same collectives (the hologram sum here)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from complex_valued_holographic_radiance_fields_b200.distributed import all_reduce_sum
+    target = torch.ones(3)
+    if rank == 0:
+        field = torch.tensor([1.0, 2.0, 3.0], requires_grad=True)
+        holo = all_reduce_sum(field * 2.0)
+    else:
+        field = torch.zeros(3, requires_grad=True)
+        holo = all_reduce_sum(field)
+    loss = ((holo - target) ** 2).mean()
+    loss.backward()
+    q.put((rank, holo.tolist(), float(loss), field.grad.tolist()))
+    dist.destroy_process_group()
+
+
+def test_idle_rank_backward_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker_idle_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    (_, h0, l0, g0), (_, h1, l1, _) = res
+    assert h0 == h1 == [2.0, 4.0, 6.0]
+    assert l0 == l1
+    expected = [2.0 * 2.0 * (2.0 * (i + 1) - 1.0) / 3.0 for i in range(3)]
+    assert all(abs(a - b) <= 1e-6 * abs(b) for a, b in zip(g0, expected))
