@@ -1,13 +1,14 @@
 """Time the reference's own CUDA kernels on one GPU (TEST INFRASTRUCTURE ONLY).
 
-Fills the per-component reference rows of BASELINE.md (B3-B7):
+Times the reference's components, one JSON line each:
 
 * B3: Rasterizer.forward at config 2 (100k Gaussians, 800x800, K = 3);
 * B4: the reference propagation (torch.fft cuFFT + bandlimited_propagation_{forward,backward},
   python_function.py:109-218 glue) per call, forward and backward, at config 1 (S = 1024),
   config 3 (S = 800) and config 4 (S = 1920, field 1080x1920);
 * B5: the full config-3 training step on the reference kernels (oracle/ref_step.py);
-* B6: adamUpdate (conv.cu:1230-1246) over the 7 parameter groups of config 3, all rows visible.
+* B6: adamUpdate (conv.cu:1230-1246) over the 6 two-dimensional parameter groups of config 3
+  (the 1-D opacity group is a dense torch Adam in the reference), all rows visible.
 
 With CVHRF_REF_DIR=oracle/_ref80 (built by `python oracle/build_ref.py --ptx80`) the same
 runs use the compute_80 PTX build JIT-compiled by the driver (B7).  Times are CUDA events,
